@@ -1,0 +1,106 @@
+// Shared helpers for libgpt_b200: status plumbing, dtype traits, device
+// error word, small math. Included once by libgpt_b200.cu, the single
+// translation unit of the library.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string>
+
+#include "../../include/gpt_b200.h"
+
+namespace gpt {
+
+// ---- host-side error reporting (thread-local last error) -------------------
+void set_error(const std::string& msg);
+int fail(int status, const char* fmt, ...);
+
+#define GPT_CHECK_ARG(cond, ...)                                   \
+  do {                                                             \
+    if (!(cond)) return ::gpt::fail(GPT_ERR_ARG, __VA_ARGS__);     \
+  } while (0)
+#define GPT_CHECK_SHAPE(cond, ...)                                 \
+  do {                                                             \
+    if (!(cond)) return ::gpt::fail(GPT_ERR_SHAPE, __VA_ARGS__);   \
+  } while (0)
+#define GPT_CHECK_ALIGN(cond, ...)                                 \
+  do {                                                             \
+    if (!(cond)) return ::gpt::fail(GPT_ERR_ALIGN, __VA_ARGS__);   \
+  } while (0)
+#define GPT_CHECK_DTYPE(dt)                                                     \
+  do {                                                                          \
+    if ((dt) != GPT_F32 && (dt) != GPT_BF16)                                    \
+      return ::gpt::fail(GPT_ERR_DTYPE, "unsupported dtype %d", (int)(dt));     \
+  } while (0)
+
+// Checks the launch that was just issued; returns GPT_OK or GPT_ERR_CUDA.
+int launch_status(const char* what);
+
+inline bool aligned(const void* p, size_t a) {
+  return (reinterpret_cast<uintptr_t>(p) % a) == 0;
+}
+
+int device_sm_count();
+
+// ---- device error word ----------------------------------------------------
+// Bounded waits and index checks record a code here instead of trapping.
+// Host reads and clears it with gpt_device_error(). The library is one
+// translation unit (libgpt_b200.cu includes every kernel file), so this is
+// a single device symbol.
+#define GPT_DEVERR_TIMEOUT 0x1u
+#define GPT_DEVERR_INDEX 0x2u
+__device__ unsigned int g_dev_error;
+__device__ __forceinline__ void record_device_error(unsigned int code) {
+  atomicOr(&g_dev_error, code);
+}
+
+// ---- dtype traits ----------------------------------------------------------
+template <typename T> struct Tr;
+template <> struct Tr<float> {
+  static __device__ __forceinline__ float to_f(float v) { return v; }
+  static __device__ __forceinline__ float from_f(float v) { return v; }
+};
+template <> struct Tr<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float v) { return __float2bfloat16_rn(v); }
+};
+
+// tanh-GELU of GPT-2 (cutile_gpt/kernels/gelu.py:16-17, :36-38):
+// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))). tanh is CUDA's tanhf
+// (accurate to a few ulp) for fp32 work; the bf16 path uses the hardware
+// tanh.approx.f32 instruction (max rel. error ~2^-11, far below bf16's 2^-8).
+__device__ __forceinline__ float tanh_fast(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+template <bool kFast>
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
+  const float k1 = 0.044715f;
+  float inner = k0 * fmaf(k1 * x, x * x, x);
+  float t = kFast ? tanh_fast(inner) : tanhf(inner);
+  return 0.5f * x * (1.0f + t);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+}  // namespace gpt
+

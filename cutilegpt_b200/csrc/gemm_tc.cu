@@ -1,0 +1,425 @@
+// bf16 dense contraction on the 5th-generation tensor cores (sm_100a):
+//   C[M, N] = epilogue(A[M, K] · W[N, K]ᵀ)
+// A is the activation (row stride lda), W the nn.Linear [out, in] weight.
+// Both operands are K-major, which is the layout tcgen05.mma consumes
+// directly, so no transposed weight copy exists (the reference keeps a
+// second [in, out] copy of every weight, cutile_gpt/models/gpt.py:83-90).
+//
+// Structure (one persistent CTA per SM, 320 threads):
+//   warp 0      TMA producer: A/W k-blocks (128 B rows, 128 B swizzle)
+//               into a kStages-deep shared-memory ring, mbarrier tx counts.
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma (M=128, N=BN,
+//               K=16 per instruction, fp32 accumulators in TMEM) and
+//               tcgen05.commit to release ring slots / publish tiles.
+//   warps 2-9   epilogue: tcgen05.ld 32 columns at a time, transpose
+//               through shared memory so each warp store covers a
+//               contiguous row segment, apply bias / GELU / residual,
+//               convert, store. Two TMEM accumulators (2 × BN columns) let
+//               the epilogue of tile i overlap the MMAs of tile i+1.
+// Every mbarrier wait is bounded (kWaitLimitNs); on expiry the kernel
+// records GPT_DEVERR_TIMEOUT and unwinds instead of spinning forever.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace gpt {
+namespace tc {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B-swizzle row
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = (2 + kEpiWarps) * 32;
+constexpr int kStageRowPitch = 33;  // fp32 words per staged row (bank-conflict free)
+constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
+
+struct Params {
+  int M, N, K;
+  int num_m, num_n, num_tiles, num_kb;
+  const __nv_bfloat16* bias;
+  const __nv_bfloat16* resid;
+  __nv_bfloat16* C;
+  int64_t ldr, ldc;
+};
+
+// ---- PTX wrappers -----------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with the given parity to complete.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try(bar, parity)) return true;
+  uint64_t t0 = global_timer_ns();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitLimitNs) {
+      record_device_error(GPT_DEVERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x,
+                                            int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accum) {
+  uint32_t mask0 = 0, mask1 = 0, mask2 = 0, mask3 = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(mask0), "r"(mask1), "r"(mask2), "r"(mask3));
+}
+// 32 lanes x 32 consecutive fp32 columns: thread t of the warp receives
+// row (quadrant*32 + t), columns [col, col+32).
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, K-major operand with 128-byte swizzle:
+// rows of 128 B, 8-row swizzle atoms 1024 B apart (stride byte offset),
+// descriptor version 1 (bits 46-47), layout type 2 = SWIZZLE_128B.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1 << 46;             // version
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major.
+template <int N_>
+__device__ __forceinline__ constexpr uint32_t idesc_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N_ >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+template <int BN>
+struct Smem {
+  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kABytes = BM * BK * 2;
+  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kRingBytes = kStages * kStageBytes;
+  static constexpr int kEpiBytes = kEpiWarps * 32 * kStageRowPitch * 4;
+  static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
+  static constexpr int kTotal = 1024 + kRingBytes + kEpiBytes + kBarBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+};
+
+template <int BN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const Params p) {
+  using S = Smem<BN>;
+  constexpr int kStages = S::kStages;
+  extern __shared__ uint8_t smem_dyn[];
+  // 1024-byte alignment is required by the 128B swizzle atoms.
+  uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
+  uint8_t* ringA = base;
+  uint8_t* ringB = base + kStages * S::kABytes;
+  float* epi = (float*)(base + S::kRingBytes);
+  uint64_t* bars = (uint64_t*)(base + S::kRingBytes + S::kEpiBytes);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kStages;
+  uint64_t* tfull = bars + 2 * kStages;
+  uint64_t* tempty = bars + 2 * kStages + 2;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kStages + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_addr(&full[s]), 1);
+      mbar_init(smem_addr(&empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_addr(&tfull[a]), 1);
+      mbar_init(smem_addr(&tempty[a]), kEpiWarps);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_addr(tmem_slot)),
+                 "r"((uint32_t)S::kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile % p.num_m;
+        const int n_blk = tile / p.num_m;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) { ok = false; break; }
+          const uint32_t fb = smem_addr(&full[stage]);
+          mbar_expect_tx(fb, S::kStageBytes);
+          tma_load_2d(smem_addr(ringA + stage * S::kABytes), &tmA, fb, kb * BK, m_blk * BM);
+          tma_load_2d(smem_addr(ringB + stage * S::kBBytes), &tmB, fb, kb * BK, n_blk * BN);
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16<BN>();
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(smem_addr(&tempty[acc]), acc_phase ^ 1)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(smem_addr(&full[stage]), phase)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t ad = desc_sw128(smem_addr(ringA + stage * S::kABytes));
+          const uint64_t bd = desc_sw128(smem_addr(ringB + stage * S::kBBytes));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 bytes per K=16 step inside the swizzle atom (encoded >>4).
+            tc_mma(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+          }
+          tc_commit(smem_addr(&empty[stage]));  // slot free once these MMAs retire
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(smem_addr(&tfull[acc]));  // accumulator ready for the epilogue
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int ew = warp - 2;             // 0..7
+    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+    const int half = ew >> 2;            // which half of the BN columns
+    float* stg = epi + ew * 32 * kStageRowPitch;
+    constexpr int kChunks = BN / 32;
+    constexpr int kChunksPerHalf = kChunks / 2;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int m_blk = tile % p.num_m;
+      const int n_blk = tile / p.num_m;
+      if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
+      tc_fence_after();
+      const int row0 = m_blk * BM + quad * 32;
+      for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
+        uint32_t r[32];
+        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32);
+        tmem_ld32(taddr, r);
+        // lane == row: stage the raw accumulators.
+#pragma unroll
+        for (int j = 0; j < 32; ++j) stg[lane * kStageRowPitch + j] = __uint_as_float(r[j]);
+        __syncwarp();
+        // lane == column: bias / GELU / residual, coalesced row stores.
+        const int col = n_blk * BN + c * 32 + lane;
+        const bool col_ok = col < p.N;
+        float bcol = 0.f;
+        if (EPI != GPT_EPI_NONE && col_ok) bcol = __bfloat162float(p.bias[col]);
+#pragma unroll 4
+        for (int rr = 0; rr < 32; ++rr) {
+          const int row = row0 + rr;
+          if (row < p.M && col_ok) {
+            float v = stg[rr * kStageRowPitch + lane] + bcol;
+            if (EPI == GPT_EPI_BIAS_GELU) v = gelu_tanh<true>(v);
+            if (EPI == GPT_EPI_BIAS_RESIDUAL) v += __bfloat162float(p.resid[(int64_t)row * p.ldr + col]);
+            p.C[(int64_t)row * p.ldc + col] = __float2bfloat16_rn(v);
+          }
+        }
+        __syncwarp();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                 "r"((uint32_t)S::kTmemCols));
+  }
+}
+
+// ---- host side ---------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (PFN_cuTensorMapEncodeTiled_v12000)ptr;
+    else
+      cudaGetLastError();
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row pitch
+// `ld` elements; box = box_rows x 64 columns, 128-byte swizzle, OOB -> 0.
+static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
+                    int box_rows) {
+  auto enc = get_encode();
+  if (!enc) return fail(GPT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(GPT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return GPT_OK;
+}
+
+template <int BN, int EPI>
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
+                     cudaStream_t st) {
+  using S = Smem<BN>;
+  static_assert(S::kTotal <= 232448, "shared memory budget exceeded");
+  auto kern = gemm_tc_kernel<BN, EPI>;
+  // Attribute set per device the first time this instantiation runs there.
+  static bool done[64] = {false};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  {
+    std::lock_guard<std::mutex> g(mu);
+    if (dev >= 0 && dev < 64 && !done[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+      if (e != cudaSuccess) return fail(GPT_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      done[dev] = true;
+    }
+  }
+  kern<<<grid, kThreads, S::kTotal, st>>>(ta, tb, p);
+  return launch_status("gemm_tc");
+}
+
+// Picks BN in {128, 256} minimising (waves x BN), i.e. the busiest SM's
+// MMA work under persistent scheduling.
+static int pick_bn(int64_t M, int64_t N, int sms) {
+  int64_t nm = (M + BM - 1) / BM;
+  int64_t t256 = nm * ((N + 255) / 256), t128 = nm * ((N + 127) / 128);
+  int64_t c256 = ((t256 + sms - 1) / sms) * 256, c128 = ((t128 + sms - 1) / sms) * 128;
+  return (N <= 128 || c128 < c256) ? 128 : 256;
+}
+
+int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const void* R, int64_t ldr,
+              void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t st) {
+  int sms = device_sm_count();
+  if (sms <= 0) return fail(GPT_ERR_CUDA, "no CUDA device");
+  int bn = pick_bn(M, N, sms);
+  CUtensorMap ta, tb;
+  int s = make_map(&ta, A, M, K, lda, BM);
+  if (s) return s;
+  s = make_map(&tb, W, N, K, K, bn);
+  if (s) return s;
+  Params p;
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_n = (int)((N + bn - 1) / bn);
+  p.num_tiles = p.num_m * p.num_n;
+  p.num_kb = (int)((K + BK - 1) / BK);
+  p.bias = (const __nv_bfloat16*)bias;
+  p.resid = (const __nv_bfloat16*)R;
+  p.C = (__nv_bfloat16*)C;
+  p.ldr = ldr;
+  p.ldc = ldc;
+  int grid = p.num_tiles < sms ? p.num_tiles : sms;
+#define GPT_TC_EPI(BNV)                                                         \
+  switch (epi) {                                                                \
+    case GPT_EPI_NONE: return launch_bn<BNV, GPT_EPI_NONE>(ta, tb, p, grid, st); \
+    case GPT_EPI_BIAS: return launch_bn<BNV, GPT_EPI_BIAS>(ta, tb, p, grid, st); \
+    case GPT_EPI_BIAS_GELU: return launch_bn<BNV, GPT_EPI_BIAS_GELU>(ta, tb, p, grid, st); \
+    default: return launch_bn<BNV, GPT_EPI_BIAS_RESIDUAL>(ta, tb, p, grid, st); \
+  }
+  if (bn == 256) {
+    GPT_TC_EPI(256)
+  } else {
+    GPT_TC_EPI(128)
+  }
+#undef GPT_TC_EPI
+}
+
+// Whether the tensor-core path can serve this request (TMA: 16-byte
+// aligned base addresses and row pitches).
+bool tc_eligible(const void* A, int64_t lda, const void* W, int64_t K, int64_t M, int64_t N) {
+  return aligned(A, 16) && aligned(W, 16) && (lda * 2) % 16 == 0 && (K * 2) % 16 == 0 && K > 0 &&
+         M > 0 && N > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31);
+}
+
+}  // namespace tc
+}  // namespace gpt

@@ -1,0 +1,391 @@
+"""CutileGPT on the sm_100a kernels — the drop-in for cutile_gpt/models/gpt.py.
+
+Same public surface as the reference class (cutile_gpt/models/gpt.py:24-343):
+``CutileGPT(config)``, ``weights`` dict with the same keys, ``forward(idx) ->
+(logits, None)``, ``generate(idx, max_new_tokens, temperature, top_k)``,
+``load_from_huggingface`` and ``load_from_mingpt``. Tensors are torch CUDA
+tensors (CuPy arrays are accepted through DLPack).
+
+What runs differently (all on libgpt_b200 kernels, no torch compute ops on
+the forward path):
+  * one fused token+position embedding kernel (gpt.py:110-113);
+  * QKV GEMM output [B, T, 3C] is read in place by the attention kernel,
+    whose output [B, T, C] feeds c_proj directly (no split/transpose copies,
+    gpt.py:133-146);
+  * bias, tanh-GELU and the residual add are GEMM epilogues (gpt.py:125-174);
+  * weights are stored once in the [out, in] layout the tensor-core GEMM
+    reads (no cached transposes, gpt.py:83-90);
+  * generate() keeps a KV cache: one prefill, then per token a decode step
+    (M = batch GEMMs, split-KV attention, lm_head on the last position only)
+    captured once in a CUDA graph and replayed. The reference re-runs the
+    whole prefix each step (gpt.py:204-206). Past block_size the reference
+    re-encodes the last block_size tokens at positions 0.. (gpt.py:205); that
+    windowed re-prefill is reproduced exactly by the non-cached path.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Optional, Tuple
+
+import torch
+
+from .. import _lib as L
+from ..kernels import ops
+from ..kernels._common import as_cuda
+from .config import GPTConfig
+from .init import init_state, weight_names
+
+
+class _Workspace:
+    """Activation buffers for one (B, T) prefill shape."""
+
+    def __init__(self, cfg: GPTConfig, B: int, T: int, dtype, device):
+        M, C = B * T, cfg.n_embd
+        self.B, self.T = B, T
+        self.x = torch.empty((M, C), dtype=dtype, device=device)       # residual stream
+        self.h = torch.empty((M, C), dtype=dtype, device=device)       # LayerNorm output
+        self.qkv = torch.empty((M, 3 * C), dtype=dtype, device=device)
+        self.att = torch.empty((M, C), dtype=dtype, device=device)
+        self.f = torch.empty((M, 4 * C), dtype=dtype, device=device)   # MLP hidden
+
+
+class _DecodeState:
+    """Buffers of the KV-cache generation loop for one (B, Tmax)."""
+
+    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device):
+        C, H = cfg.n_embd, cfg.n_head
+        D = C // H
+        self.B, self.Tmax = B, Tmax
+        self.cache = torch.empty((cfg.n_layer, 2, B, H, Tmax, D), dtype=dtype, device=device)
+        self.x = torch.empty((B, C), dtype=dtype, device=device)
+        self.h = torch.empty((B, C), dtype=dtype, device=device)
+        self.qkv = torch.empty((B, 3 * C), dtype=dtype, device=device)
+        self.att = torch.empty((B, C), dtype=dtype, device=device)
+        self.f = torch.empty((B, 4 * C), dtype=dtype, device=device)
+        self.logits = torch.empty((B, cfg.vocab_size), dtype=dtype, device=device)
+        self.tok = torch.empty((B,), dtype=torch.int64, device=device)
+        self.pos = torch.zeros((1,), dtype=torch.int64, device=device)
+        nbytes = ops.decode_workspace_bytes(B, H, D, Tmax)
+        self.dec_ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=device)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.graph_seq = None
+
+
+class CutileGPT:
+    """GPT-2 inference model on hand-written sm_100a kernels."""
+
+    def __init__(self, config: GPTConfig, dtype: torch.dtype = torch.float32,
+                 device: Optional[torch.device | str] = None, seed: Optional[int] = None):
+        self.config = config
+        self.dtype = dtype
+        self.device = torch.device(device) if device is not None else torch.device('cuda')
+        self.weights: Dict[str, torch.Tensor] = {}
+        # The reference caches [in, out] copies of every weight (gpt.py:83-90);
+        # the tensor-core GEMM reads [out, in] directly, so this stays empty.
+        self.weight_transposes: Dict[str, torch.Tensor] = {}
+        self._ws: Dict[Tuple[int, int], _Workspace] = {}
+        self._dec: Dict[Tuple[int, int], _DecodeState] = {}
+        self._init_weights(seed)
+
+    # ------------------------------------------------------------------ weights
+    def _init_weights(self, seed: Optional[int] = None):
+        """Random init with the reference's distributions (gpt.py:39-81)."""
+        if seed is None:
+            seed = int(torch.randint(0, 2**31 - 1, (1,)).item())
+        self.load_state(init_state(self.config, seed))
+
+    def load_state(self, state: Dict[str, torch.Tensor]) -> None:
+        """Installs a weight dict in the reference key layout (Linear weights [out, in]).
+
+        ``lm_head.weight`` stays tied to ``wte`` when both entries are the same
+        tensor (or equal); otherwise it is stored separately, as minGPT's
+        untied head is (gpt.py:340).
+        """
+        cfg = self.config
+        missing = [k for k in weight_names(cfg) if k not in state]
+        if missing:
+            raise KeyError(f"missing weights: {missing[:5]}{'...' if len(missing) > 5 else ''}")
+        self._check_shapes(state)
+        conv = {}
+        for k in weight_names(cfg):
+            if k == 'lm_head.weight':
+                continue
+            conv[k] = state[k].detach().to(device=self.device, dtype=self.dtype).contiguous()
+        lm = state['lm_head.weight']
+        tied = lm is state['wte'] or (lm.shape == state['wte'].shape and
+                                      lm.data_ptr() == state['wte'].data_ptr())
+        conv['lm_head.weight'] = conv['wte'] if tied else lm.detach().to(
+            device=self.device, dtype=self.dtype).contiguous()
+        self.weights = conv
+        self._dec.clear()
+
+    def _check_shapes(self, state):
+        cfg = self.config
+        C, V = cfg.n_embd, cfg.vocab_size
+        want = {'wte': (V, C), 'wpe': (cfg.block_size, C), 'lm_head.weight': (V, C),
+                'ln_f.weight': (C,), 'ln_f.bias': (C,)}
+        for i in range(cfg.n_layer):
+            p = f'h.{i}.'
+            want.update({p + 'attn.c_attn.weight': (3 * C, C), p + 'attn.c_attn.bias': (3 * C,),
+                         p + 'attn.c_proj.weight': (C, C), p + 'attn.c_proj.bias': (C,),
+                         p + 'mlp.c_fc.weight': (4 * C, C), p + 'mlp.c_fc.bias': (4 * C,),
+                         p + 'mlp.c_proj.weight': (C, 4 * C), p + 'mlp.c_proj.bias': (C,),
+                         p + 'ln_1.weight': (C,), p + 'ln_1.bias': (C,), p + 'ln_2.weight': (C,),
+                         p + 'ln_2.bias': (C,)})
+        for k, shp in want.items():
+            if tuple(state[k].shape) != shp:
+                raise ValueError(f"weight {k}: shape {tuple(state[k].shape)} != expected {shp}")
+
+    def _w(self, key: str) -> torch.Tensor:
+        return self.weights[key]
+
+    # ------------------------------------------------------------------ forward
+    def __call__(self, idx) -> Tuple[torch.Tensor, None]:
+        return self.forward(idx)
+
+    def _workspace(self, B: int, T: int) -> _Workspace:
+        key = (B, T)
+        ws = self._ws.get(key)
+        if ws is None:
+            if len(self._ws) >= 4:  # bounded cache of activation buffers
+                self._ws.pop(next(iter(self._ws)))
+            ws = _Workspace(self.config, B, T, self.dtype, self.device)
+            self._ws[key] = ws
+        return ws
+
+    def _blocks(self, idx: torch.Tensor, ws: _Workspace, cache: Optional[torch.Tensor] = None) -> None:
+        """Embedding, all transformer blocks and ln_f; result in ws.h. Appends K/V to `cache`."""
+        cfg = self.config
+        B, T = idx.shape
+        C, H = cfg.n_embd, cfg.n_head
+        D = C // H
+        scale = 1.0 / math.sqrt(D)
+        ops.embedding_pos(idx, self._w('wte'), self._w('wpe'), ws.x)
+        qkv4 = ws.qkv.view(B, T, 3, H, D)
+        q, k, v = (qkv4[:, :, j].transpose(1, 2) for j in range(3))    # [B, H, T, D] views
+        att4 = ws.att.view(B, T, H, D).transpose(1, 2)
+        for i in range(cfg.n_layer):
+            p = f'h.{i}.'
+            ops.layernorm(ws.x, self._w(p + 'ln_1.weight'), self._w(p + 'ln_1.bias'), ws.h)
+            ops.gemm(ws.h, self._w(p + 'attn.c_attn.weight'), ws.qkv, bias=self._w(p + 'attn.c_attn.bias'))
+            if cache is not None:
+                ops.kv_append(ws.qkv.view(B, T, 3 * C), cache[i, 0], cache[i, 1], pos0=0)
+            ops.attention_prefill(q, k, v, att4, scale)
+            ops.gemm(ws.att, self._w(p + 'attn.c_proj.weight'), ws.x, bias=self._w(p + 'attn.c_proj.bias'),
+                     resid=ws.x)
+            ops.layernorm(ws.x, self._w(p + 'ln_2.weight'), self._w(p + 'ln_2.bias'), ws.h)
+            ops.gemm(ws.h, self._w(p + 'mlp.c_fc.weight'), ws.f, bias=self._w(p + 'mlp.c_fc.bias'),
+                     epilogue=L.EPI_BIAS_GELU)
+            ops.gemm(ws.f, self._w(p + 'mlp.c_proj.weight'), ws.x, bias=self._w(p + 'mlp.c_proj.bias'),
+                     resid=ws.x)
+        ops.layernorm(ws.x, self._w('ln_f.weight'), self._w('ln_f.bias'), ws.h)
+
+    def _prep_idx(self, idx) -> torch.Tensor:
+        idx = as_cuda(idx, "idx")
+        if idx.dim() != 2:
+            raise ValueError(f"idx must be (batch, seq_len), got shape {tuple(idx.shape)}")
+        if idx.device != self.device and self.device.index is not None:
+            idx = idx.to(self.device)
+        return idx.to(torch.int64).contiguous()
+
+    def forward(self, idx) -> Tuple[torch.Tensor, None]:
+        """Logits (batch, seq_len, vocab) in the model dtype for every position."""
+        idx = self._prep_idx(idx)
+        B, T = idx.shape
+        cfg = self.config
+        assert T <= cfg.block_size, f"Sequence length {T} > block_size {cfg.block_size}"
+        logits = torch.empty((B, T, cfg.vocab_size), dtype=self.dtype, device=self.device)
+        if B * T == 0:
+            return logits, None
+        ws = self._workspace(B, T)
+        self._blocks(idx, ws)
+        ops.gemm(ws.h, self._w('lm_head.weight'), logits.view(B * T, cfg.vocab_size))
+        return logits, None
+
+    def forward_last(self, idx, out: Optional[torch.Tensor] = None,
+                     cache: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Logits of the last position only, (batch, vocab): the prefill step of generation."""
+        idx = self._prep_idx(idx)
+        B, T = idx.shape
+        assert T <= self.config.block_size
+        ws = self._workspace(B, T)
+        self._blocks(idx, ws, cache)
+        if out is None:
+            out = torch.empty((B, self.config.vocab_size), dtype=self.dtype, device=self.device)
+        last = ws.h.view(B, T, -1)[:, T - 1, :]          # row-strided [B, C] view
+        ops.gemm(last, self._w('lm_head.weight'), out)
+        return out
+
+    # ------------------------------------------------------------------ decode
+    def _decode_state(self, B: int, Tmax: int) -> _DecodeState:
+        key = (B, Tmax)
+        st = self._dec.get(key)
+        if st is None:
+            if len(self._dec) >= 2:
+                self._dec.pop(next(iter(self._dec)))
+            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device)
+            self._dec[key] = st
+        return st
+
+    def _decode_step(self, st: _DecodeState) -> None:
+        """One token per sequence at device position *st.pos: logits into st.logits."""
+        cfg = self.config
+        C, H = cfg.n_embd, cfg.n_head
+        scale = 1.0 / math.sqrt(C // H)
+        B = st.B
+        ops.embedding_pos(st.tok.view(B, 1), self._w('wte'), self._w('wpe'), st.x, pos0=0, pos_dev=st.pos)
+        q = st.qkv[:, :C]
+        for i in range(cfg.n_layer):
+            p = f'h.{i}.'
+            ops.layernorm(st.x, self._w(p + 'ln_1.weight'), self._w(p + 'ln_1.bias'), st.h)
+            ops.gemm(st.h, self._w(p + 'attn.c_attn.weight'), st.qkv, bias=self._w(p + 'attn.c_attn.bias'))
+            ops.kv_append(st.qkv.view(B, 1, 3 * C), st.cache[i, 0], st.cache[i, 1], pos0=0, pos_dev=st.pos)
+            ops.attention_decode(q, st.cache[i, 0], st.cache[i, 1], st.att, 1, st.dec_ws, scale,
+                                 len_dev=st.pos)
+            ops.gemm(st.att, self._w(p + 'attn.c_proj.weight'), st.x, bias=self._w(p + 'attn.c_proj.bias'),
+                     resid=st.x)
+            ops.layernorm(st.x, self._w(p + 'ln_2.weight'), self._w(p + 'ln_2.bias'), st.h)
+            ops.gemm(st.h, self._w(p + 'mlp.c_fc.weight'), st.f, bias=self._w(p + 'mlp.c_fc.bias'),
+                     epilogue=L.EPI_BIAS_GELU)
+            ops.gemm(st.f, self._w(p + 'mlp.c_proj.weight'), st.x, bias=self._w(p + 'mlp.c_proj.bias'),
+                     resid=st.x)
+        ops.layernorm(st.x, self._w('ln_f.weight'), self._w('ln_f.bias'), st.h)
+        ops.gemm(st.h, self._w('lm_head.weight'), st.logits)
+
+    def _greedy_step(self, st: _DecodeState, seq: torch.Tensor) -> None:
+        self._decode_step(st)
+        ops.argmax(st.logits, st.tok)
+        ops.decode_advance(st.tok, st.pos, seq)
+
+    def _sample(self, logits: torch.Tensor, temperature: float, top_k: Optional[int],
+                generator: Optional[torch.Generator]) -> torch.Tensor:
+        """Temperature / top-k / multinomial draw (gpt.py:207-225), batched over rows."""
+        logits = logits.float() / temperature
+        if top_k is not None:
+            k = min(top_k, logits.shape[-1])
+            kth = torch.topk(logits, k, dim=-1).values[:, -1:]
+            logits = logits.masked_fill(logits < kth, float('-inf'))
+        probs = torch.softmax(logits, dim=-1)
+        return torch.multinomial(probs, 1, generator=generator).squeeze(1)
+
+    @torch.no_grad()
+    def generate(self, idx, max_new_tokens: int, temperature: float = 1.0, top_k: Optional[int] = None,
+                 use_kv_cache: bool = True, use_cuda_graph: bool = True,
+                 generator: Optional[torch.Generator] = None) -> torch.Tensor:
+        """Autoregressive generation; returns (batch, seq_len + max_new_tokens) int64.
+
+        ``top_k=1`` is greedy decoding (deterministic argmax, ties to the
+        lowest token id). Other settings sample with ``temperature`` / ``top_k``.
+        """
+        idx = self._prep_idx(idx)
+        B, T0 = idx.shape
+        cfg = self.config
+        if max_new_tokens <= 0:
+            return idx.clone()
+        total = T0 + max_new_tokens
+        greedy = top_k == 1
+        if not use_kv_cache or total > cfg.block_size:
+            return self._generate_reforward(idx, max_new_tokens, temperature, top_k, generator)
+        seq = torch.empty((B, total), dtype=torch.int64, device=self.device)
+        seq[:, :T0] = idx
+        st = self._decode_state(B, total)
+        # prefill: K/V of the prompt into the cache, logits of the last position
+        self.forward_last(idx, out=st.logits, cache=st.cache)
+        if greedy:
+            ops.argmax(st.logits, st.tok)
+        else:
+            st.tok.copy_(self._sample(st.logits, temperature, top_k, generator))
+        seq[:, T0] = st.tok
+        st.pos.fill_(T0)
+        steps = max_new_tokens - 1
+        if steps == 0:
+            return seq
+        if not greedy:
+            for _ in range(steps):
+                self._decode_step(st)
+                st.tok.copy_(self._sample(st.logits, temperature, top_k, generator))
+                ops.decode_advance(st.tok, st.pos, seq)
+            return seq
+        if not use_cuda_graph or steps < 3:
+            for _ in range(steps):
+                self._greedy_step(st, seq)
+            return seq
+        # First step eagerly (warms every kernel), then capture one step and replay.
+        self._greedy_step(st, seq)
+        self._capture(st, seq)
+        for _ in range(steps - 1):
+            st.graph.replay()
+        return seq
+
+    def _capture(self, st: _DecodeState, seq: torch.Tensor) -> None:
+        if st.graph is not None and st.graph_seq is seq:
+            return
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream(device=self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                self._greedy_step(st, seq)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        st.graph, st.graph_seq = g, seq
+
+    def _generate_reforward(self, idx, max_new_tokens, temperature, top_k, generator) -> torch.Tensor:
+        """Reference semantics without a cache: re-run the (cropped) prefix each step."""
+        cfg = self.config
+        for _ in range(max_new_tokens):
+            idx_cond = idx if idx.shape[1] <= cfg.block_size else idx[:, -cfg.block_size:].contiguous()
+            logits = self.forward_last(idx_cond)
+            if top_k == 1:
+                nxt = torch.empty((idx.shape[0],), dtype=torch.int64, device=self.device)
+                ops.argmax(logits, nxt)
+            else:
+                nxt = self._sample(logits, temperature, top_k, generator)
+            idx = torch.cat([idx, nxt.view(-1, 1)], dim=1)
+        return idx
+
+    # ------------------------------------------------------------------ loaders
+    def load_from_state_dict(self, sd: Dict[str, torch.Tensor], layout: str = 'hf') -> None:
+        """Loads a GPT-2 state dict with HF (Conv1D [in, out]) or minGPT (Linear [out, in]) layout.
+
+        Key mapping and transposes follow gpt.py:262-299 (HF) and gpt.py:316-340 (minGPT).
+        """
+        cfg = self.config
+        conv1d = layout == 'hf'
+        w: Dict[str, torch.Tensor] = {}
+
+        def get(k):
+            t = sd[k]
+            return t.detach().float().cpu() if isinstance(t, torch.Tensor) else torch.as_tensor(t).float()
+
+        w['wte'] = get('transformer.wte.weight')
+        w['wpe'] = get('transformer.wpe.weight')
+        for i in range(cfg.n_layer):
+            p, s = f'h.{i}.', f'transformer.h.{i}.'
+            for n in ('ln_1.weight', 'ln_1.bias', 'ln_2.weight', 'ln_2.bias', 'attn.c_attn.bias',
+                      'attn.c_proj.bias', 'mlp.c_fc.bias', 'mlp.c_proj.bias'):
+                w[p + n] = get(s + n)
+            for n in ('attn.c_attn.weight', 'attn.c_proj.weight', 'mlp.c_fc.weight', 'mlp.c_proj.weight'):
+                t = get(s + n)
+                w[p + n] = t.t().contiguous() if conv1d else t
+        w['ln_f.weight'] = get('transformer.ln_f.weight')
+        w['ln_f.bias'] = get('transformer.ln_f.bias')
+        if conv1d or 'lm_head.weight' not in sd:
+            w['lm_head.weight'] = w['wte']           # tied (gpt.py:299)
+        else:
+            w['lm_head.weight'] = get('lm_head.weight')
+        self.load_state(w)
+
+    def load_from_huggingface(self, model_name: str = 'gpt2'):
+        """Loads pretrained GPT-2 weights through transformers (gpt.py:231-304)."""
+        try:
+            from transformers import GPT2LMHeadModel
+        except ImportError as e:  # pragma: no cover
+            raise ImportError("load_from_huggingface requires the 'transformers' package") from e
+        hf_model = GPT2LMHeadModel.from_pretrained(model_name)
+        self.load_from_state_dict(hf_model.state_dict(), layout='hf')
+        print(f"Loaded weights from HuggingFace: {model_name}")
+
+    def load_from_mingpt(self, mingpt_model):
+        """Loads weights from a minGPT model instance (gpt.py:306-343)."""
+        self.load_from_state_dict(mingpt_model.state_dict(), layout='mingpt')
+        print("Loaded weights from minGPT")

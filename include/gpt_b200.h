@@ -1,0 +1,165 @@
+/*
+ * gpt_b200.h — C ABI of libgpt_b200.so, the sm_100a (B200) kernel library
+ * behind cutilegpt_b200's drop-in replacement of cutileGPT's kernel package.
+ *
+ * Conventions (every entry point):
+ *   - Pointers are CUDA device pointers unless stated otherwise; shapes and
+ *     strides are int64 element counts; `stream` is a cudaStream_t passed as
+ *     void* (NULL = legacy default stream).
+ *   - The library never allocates outputs and never synchronises the stream.
+ *     Kernels are launched asynchronously on `stream`.
+ *   - Return value is a gpt_status. On failure gpt_last_error_string()
+ *     (thread-local) describes the cause. No C++ exception crosses the ABI.
+ *   - dtype is a gpt_dtype value; inputs and outputs of one call share it.
+ *
+ * The Python operator each entry point replaces is cited as
+ * `file:line` inside the reference project cutileGPT (package cutile_gpt).
+ */
+#ifndef GPT_B200_H
+#define GPT_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define GPT_API __attribute__((visibility("default")))
+#else
+#define GPT_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  GPT_OK = 0,
+  GPT_ERR_SHAPE = 1,        /* inconsistent or out-of-range sizes          */
+  GPT_ERR_ALIGN = 2,        /* pointer/stride alignment the kernel needs   */
+  GPT_ERR_DTYPE = 3,        /* dtype not supported by this entry point     */
+  GPT_ERR_UNSUPPORTED = 4,  /* valid request this build cannot serve       */
+  GPT_ERR_CUDA = 5,         /* a CUDA runtime/driver call failed           */
+  GPT_ERR_TIMEOUT = 6,      /* a bounded device wait gave up               */
+  GPT_ERR_ARG = 7           /* null pointer or bad enum                    */
+} gpt_status;
+
+typedef enum { GPT_F32 = 0, GPT_BF16 = 1 } gpt_dtype;
+
+typedef enum {
+  GPT_EPI_NONE = 0,           /* C = A·Wᵀ                                  */
+  GPT_EPI_BIAS = 1,           /* C = A·Wᵀ + bias                           */
+  GPT_EPI_BIAS_GELU = 2,      /* C = gelu_tanh(A·Wᵀ + bias)                */
+  GPT_EPI_BIAS_RESIDUAL = 3   /* C = A·Wᵀ + bias + R   (C may alias R)     */
+} gpt_epilogue;
+
+/* ---- library / error state ------------------------------------------- */
+GPT_API int gpt_version(void);
+GPT_API const char* gpt_last_error_string(void);
+/* Reads and clears the device-side error word that bounded waits set when
+ * they give up (GPT_ERR_TIMEOUT). Synchronises the current device. */
+GPT_API int gpt_device_error(int* code_out);
+/* Number of SMs of the current device (0 if no device). */
+GPT_API int gpt_sm_count(void);
+
+/* ---- embedding --------------------------------------------------------- */
+/* out[i, :] = weight[idx[i], :] for i < n_idx.  Indices outside [0, vocab)
+ * produce GPT_ERR_SHAPE at the next gpt_device_error() and zero rows.
+ * Replaces cutile_embedding  (cutile_gpt/kernels/embedding.py:54-109). */
+GPT_API int gpt_embedding(const int64_t* idx, int64_t n_idx, const void* weight,
+                  int64_t vocab, int64_t C, void* out, int dtype, void* stream);
+
+/* out[b, t, :] = wte[idx[b, t], :] + wpe[p0 + t, :] — the token +
+ * position embedding and broadcast add of CutileGPT.forward
+ * (cutile_gpt/models/gpt.py:110-113) in one pass. idx is [B, T] contiguous.
+ * p0 = pos0 + (pos_dev ? *pos_dev : 0): pos_dev is an optional device-side
+ * position so a captured decode step can advance without new arguments.
+ * Out-of-range token ids or positions give zero rows and are reported by
+ * gpt_device_error(). */
+GPT_API int gpt_embedding_pos(const int64_t* idx, int64_t B, int64_t T,
+                      const void* wte, const void* wpe, int64_t vocab,
+                      int64_t n_pos, int64_t C, int64_t pos0,
+                      const int64_t* pos_dev, void* out, int dtype,
+                      void* stream);
+
+/* ---- layernorm --------------------------------------------------------- */
+/* y[m, :] = (x[m, :] - mean) * rsqrt(var + eps) * w + b over rows of length
+ * C (contiguous rows). Statistics in fp32. y may alias x.
+ * Replaces cutile_layer_norm (cutile_gpt/kernels/layernorm.py:77-135). */
+GPT_API int gpt_layernorm(const void* x, const void* w, const void* b, void* y,
+                  int64_t M, int64_t C, float eps, int dtype, void* stream);
+
+/* ---- gelu -------------------------------------------------------------- */
+/* y = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))), n elements, y may
+ * alias x. Replaces cutile_gelu (cutile_gpt/kernels/gelu.py:71-110). */
+GPT_API int gpt_gelu(const void* x, void* y, int64_t n, int dtype, void* stream);
+
+/* ---- dense contraction -------------------------------------------------- */
+/* C[m, n] = epilogue(sum_k A[m, k] * W[n, k]) with A [M, K] (row stride lda),
+ * W [N, K] (the nn.Linear [out, in] layout, contiguous), C [M, N] (row
+ * stride ldc), R [M, N] (row stride ldr).  bf16: tcgen05/TMEM tensor-core
+ * kernel fed by TMA, fp32 accumulation; f32: fp32 CUDA-core kernel.
+ * Replaces cutile_linear / cutile_linear_bias
+ * (cutile_gpt/kernels/linear.py:112-161, :164-222) and the residual adds
+ * of CutileGPT.forward (cutile_gpt/models/gpt.py:155, :174). */
+GPT_API int gpt_gemm(const void* A, int64_t lda, const void* W, const void* bias,
+             const void* R, int64_t ldr, void* C, int64_t ldc, int64_t M,
+             int64_t N, int64_t K, int epilogue, int dtype, void* stream);
+
+/* ---- attention ----------------------------------------------------------- */
+/* Causal softmax(q kᵀ * scale) v for every (b, h).  Element (b, h, t, d) of
+ * tensor X lives at X + b*sb + h*sh + t*st + d (d contiguous); q, k, v and
+ * out each carry their own strides so both the [B, H, T, D] layout of the
+ * reference API and the fused [B, T, 3C] QKV-buffer layout are served
+ * without copies. Replaces cutile_causal_attention
+ * (cutile_gpt/kernels/attention.py:119-175). */
+GPT_API int gpt_attention_prefill(const void* q, const void* k, const void* v,
+                          void* out, int64_t B, int64_t H, int64_t T,
+                          int64_t D, const int64_t* q_strides,
+                          const int64_t* k_strides, const int64_t* v_strides,
+                          const int64_t* o_strides, float scale, int dtype,
+                          void* stream);
+
+/* ---- KV cache + decode (no reference counterpart: the reference re-runs
+ * the full forward per generated token, cutile_gpt/models/gpt.py:204-206) */
+/* Copies K and V of Tn new positions from a [B, Tn, 3C] QKV buffer (row
+ * stride ld_qkv) into k_cache/v_cache [B, H, Tmax, D] at positions
+ * p0..p0+Tn-1, p0 = pos0 + (pos_dev ? *pos_dev : 0). Positions past Tmax
+ * are dropped and reported by gpt_device_error(). */
+GPT_API int gpt_kv_append(const void* qkv, int64_t ld_qkv, void* k_cache,
+                  void* v_cache, int64_t B, int64_t H, int64_t Tn,
+                  int64_t D, int64_t Tmax, int64_t pos0,
+                  const int64_t* pos_dev, int dtype, void* stream);
+
+/* Bytes of workspace gpt_attention_decode needs when the attended length
+ * is at most L (size it with L = Tmax to cover every decode step). */
+GPT_API int64_t gpt_attention_decode_workspace_size(int64_t B, int64_t H, int64_t D,
+                                            int64_t L);
+
+/* One-query attention per (b, h) over the first Leff cached positions,
+ * Leff = L + (len_dev ? *len_dev : 0):
+ * out[b, h*D + d] = softmax(q·Kᵀ * scale) V.  q is read from
+ * q + b*ld_q + h*D, the caches are [B, H, Tmax, D], out is [B, H*D] with
+ * row stride ld_out. Split over the KV length (flash-decoding); partials go
+ * to `workspace` (gpt_attention_decode_workspace_size(B, H, D, Lsplit)
+ * bytes, Lsplit = L without len_dev and Tmax with it; may be NULL when
+ * that size is 0). */
+GPT_API int gpt_attention_decode(const void* q, int64_t ld_q, const void* k_cache,
+                         const void* v_cache, void* out, int64_t ld_out,
+                         int64_t B, int64_t H, int64_t D, int64_t Tmax,
+                         int64_t L, const int64_t* len_dev, float scale,
+                         void* workspace, int dtype, void* stream);
+
+/* End of a decode step: seq[b, *pos_dev + 1] = tok[b] for b < B (seq row
+ * stride ld_seq, skipped when seq is NULL), then *pos_dev += 1. Positions
+ * at or past seq_len are not written. One tiny kernel. */
+GPT_API int gpt_decode_advance(const int64_t* tok, int64_t B, int64_t* seq,
+                       int64_t ld_seq, int64_t seq_len, int64_t* pos_dev,
+                       void* stream);
+
+/* out[b] = argmax_v logits[b, v] (first index on ties), logits row stride
+ * ld. Greedy step of generate(top_k=1) (cutile_gpt/models/gpt.py:207-225). */
+GPT_API int gpt_argmax(const void* logits, int64_t ld, int64_t B, int64_t V,
+               int64_t* out, int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GPT_B200_H */

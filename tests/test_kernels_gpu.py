@@ -1,0 +1,278 @@
+"""Per-kernel parity of libgpt_b200 against the fp64 CPU oracle and the golden fixtures.
+
+Tolerances: fp32 kernels follow the reference self-tests (layernorm / linear
+1e-4, gelu 1e-5, attention 1e-3: cutile_gpt/kernels/*.py __main__ blocks);
+bf16 kernels are compared with the oracle run on the same bf16-rounded
+inputs, within a relative error of 2e-2 (max|Δ| / max|ref|).
+"""
+import math
+
+import pytest
+import torch
+
+from oracle import ref_gpt as R
+from cutilegpt_b200 import _lib as L
+from cutilegpt_b200.kernels import ops
+import cutilegpt_b200 as cg
+
+pytestmark = pytest.mark.gpu
+BF16_REL = 2e-2
+
+
+def rel_err(got, ref):
+    got, ref = got.double().cpu(), ref.double().cpu()
+    return ((got - ref).abs().max() / ref.abs().max().clamp_min(1e-30)).item()
+
+
+def randn(*shape, seed=0, dtype=torch.float32, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g, dtype=torch.float64) * scale).to(dtype)
+
+
+def cuda(t):
+    return t.cuda()
+
+
+# ----------------------------------------------------------------- golden cases
+def test_golden_layernorm_fp32(golden):
+    c = golden["kernels"]["layernorm"]
+    y = cg.cutile_layer_norm(cuda(c["x"]), cuda(c["w"]), cuda(c["b"]))
+    torch.testing.assert_close(y.cpu(), c["y"], atol=1e-4, rtol=1e-4)
+
+
+@pytest.mark.parametrize("name", ["gelu_1d", "gelu_2d", "gelu_3d"])
+def test_golden_gelu_fp32(golden, name):
+    c = golden["kernels"][name]
+    y = cg.cutile_gelu(cuda(c["x"]))
+    torch.testing.assert_close(y.cpu(), c["y"], atol=1e-5, rtol=1e-5)
+
+
+def test_golden_linear_fp32(golden):
+    c = golden["kernels"]["linear"]
+    y = cg.cutile_linear(cuda(c["x"]), cuda(c["w"]))
+    yb = cg.cutile_linear_bias(cuda(c["x"]), cuda(c["w"]), cuda(c["b"]))
+    torch.testing.assert_close(y.cpu(), c["y"], atol=1e-4, rtol=1e-4)
+    torch.testing.assert_close(yb.cpu(), c["y_bias"], atol=1e-4, rtol=1e-4)
+
+
+def test_golden_attention_fp32(golden):
+    c = golden["kernels"]["attention"]
+    y = cg.cutile_causal_attention(cuda(c["q"]), cuda(c["k"]), cuda(c["v"]), 3)
+    torch.testing.assert_close(y.cpu(), c["y"], atol=1e-3, rtol=1e-3)
+
+
+# ----------------------------------------------------------------- layernorm
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("M,C", [(1, 48), (130, 48), (257, 384), (64, 768), (33, 1600), (5, 100), (3, 8200)])
+def test_layernorm(dtype, M, C):
+    x = randn(M, C, seed=1, scale=3.0) + 0.5
+    w, b = randn(C, seed=2) * 0.1 + 1.0, randn(C, seed=3) * 0.1
+    xd, wd, bd = (t.to(dtype) for t in (x, w, b))
+    y = cg.cutile_layer_norm(cuda(xd), cuda(wd), cuda(bd))
+    ref = R.layer_norm(xd.double(), wd.double(), bd.double())
+    if dtype == torch.float32:
+        torch.testing.assert_close(y.cpu().double(), ref, atol=1e-4, rtol=1e-4)
+    else:
+        assert rel_err(y, ref) < BF16_REL
+
+
+# ----------------------------------------------------------------- gelu
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("n", [1, 7, 1024, 12345, 32 * 512 * 768])
+def test_gelu(dtype, n):
+    x = randn(n, seed=4, scale=3.0).to(dtype)
+    y = cg.cutile_gelu(cuda(x))
+    ref = R.gelu(x.double())
+    if dtype == torch.float32:
+        torch.testing.assert_close(y.cpu().double(), ref, atol=1e-5, rtol=1e-5)
+    else:
+        # bf16 output rounding (2^-9 relative) dominates
+        torch.testing.assert_close(y.cpu().double(), ref, atol=1e-2, rtol=8e-3)
+
+
+def test_gelu_unaligned_view():
+    x = randn(1001, seed=5).cuda()
+    y = torch.empty_like(x)
+    ops.gelu(x[1:], y[1:])
+    torch.testing.assert_close(y[1:].cpu().double(), R.gelu(x[1:].cpu().double()), atol=1e-5, rtol=1e-5)
+
+
+# ----------------------------------------------------------------- embedding
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("C", [48, 768, 1600, 100])
+def test_embedding(dtype, C):
+    V, B, T = 1000, 3, 37
+    wte, wpe = randn(V, C, seed=6).to(dtype), randn(64, C, seed=7).to(dtype)
+    idx = torch.randint(0, V, (B, T), generator=torch.Generator().manual_seed(8))
+    e = cg.cutile_embedding(idx.cuda(), wte.cuda())
+    assert e.shape == (B, T, C)
+    assert torch.equal(e.cpu(), wte[idx])
+    out = torch.empty((B, T, C), dtype=dtype, device="cuda")
+    ops.embedding_pos(idx.cuda(), wte.cuda(), wpe.cuda(), out, pos0=5)
+    ref = (wte.double()[idx] + wpe.double()[5:5 + T].unsqueeze(0)).to(dtype)
+    assert torch.equal(out.cpu(), ref)
+
+
+def test_embedding_out_of_range_reports():
+    w = randn(10, 16, seed=9).cuda()
+    idx = torch.tensor([[1, 12]], device="cuda")
+    out = cg.cutile_embedding(idx, w)
+    with pytest.raises(L.GptError):
+        L.device_error()
+    assert torch.all(out[0, 1] == 0)
+    assert L.device_error() == 0  # cleared
+
+
+# ----------------------------------------------------------------- gemm
+EPIS = [L.EPI_NONE, L.EPI_BIAS, L.EPI_BIAS_GELU, L.EPI_BIAS_RESIDUAL]
+
+
+def gemm_ref(a, w, bias, r, epi):
+    y = a.double() @ w.double().t()
+    if epi != L.EPI_NONE:
+        y = y + bias.double()
+    if epi == L.EPI_BIAS_GELU:
+        y = R.gelu(y)
+    if epi == L.EPI_BIAS_RESIDUAL:
+        y = y + r.double()
+    return y
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("epi", EPIS)
+@pytest.mark.parametrize("M,N,K", [(64, 192, 48), (128, 256, 64), (200, 2304, 768), (300, 768, 3072),
+                                   (129, 50257, 48), (64, 3072, 768), (8, 768, 768), (1000, 129, 1600)])
+def test_gemm(dtype, epi, M, N, K):
+    a = randn(M, K, seed=10).to(dtype)
+    w = (randn(N, K, seed=11) / math.sqrt(K)).to(dtype)
+    bias = randn(N, seed=12).to(dtype)
+    r = randn(M, N, seed=13).to(dtype)
+    out = torch.empty((M, N), dtype=dtype, device="cuda")
+    ops.gemm(a.cuda(), w.cuda(), out, bias=bias.cuda(), resid=r.cuda() if epi == L.EPI_BIAS_RESIDUAL else None,
+             epilogue=epi)
+    ref = gemm_ref(a, w, bias, r, epi)
+    if dtype == torch.float32:
+        torch.testing.assert_close(out.cpu().double(), ref, atol=1e-4, rtol=1e-4)
+    else:
+        assert rel_err(out, ref) < BF16_REL, rel_err(out, ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_gemm_strided_and_inplace_residual(dtype):
+    M, N, K = 96, 384, 384
+    big = randn(M, 2 * K, seed=14).to(dtype).cuda()
+    a = big[:, 8:8 + K]                        # row stride 2K, 16-byte aligned offset
+    w = (randn(N, K, seed=15) / math.sqrt(K)).to(dtype).cuda()
+    bias = randn(N, seed=16).to(dtype).cuda()
+    x = randn(M, N, seed=17).to(dtype).cuda()
+    ref = gemm_ref(a.cpu(), w.cpu(), bias.cpu(), x.cpu(), L.EPI_BIAS_RESIDUAL)
+    ops.gemm(a, w, x, bias=bias, resid=x)      # C aliases R
+    tol = 1e-4 if dtype == torch.float32 else None
+    if tol:
+        torch.testing.assert_close(x.cpu().double(), ref, atol=tol, rtol=tol)
+    else:
+        assert rel_err(x, ref) < BF16_REL
+
+
+def test_gemm_bf16_unaligned_takes_cuda_core_path():
+    M, N, K = 40, 70, 36                       # K*2 bytes not a multiple of 16 -> no TMA
+    a, w = randn(M, K, seed=18).bfloat16(), randn(N, K, seed=19).bfloat16()
+    y = cg.cutile_linear(a.cuda(), w.cuda())
+    assert rel_err(y, a.double() @ w.double().t()) < BF16_REL
+
+
+def test_gemm_rejects_bad_args():
+    a = torch.zeros(4, 8, device="cuda")
+    w = torch.zeros(4, 8, device="cuda")
+    out = torch.zeros(4, 4, device="cuda")
+    with pytest.raises(ValueError):
+        ops.gemm(a, w, out, epilogue=L.EPI_BIAS)          # bias missing
+    with pytest.raises(ValueError):
+        ops.gemm(a, w, out, epilogue=9)
+
+
+# ----------------------------------------------------------------- attention
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,H,T,D", [(2, 3, 32, 16), (2, 4, 128, 64), (1, 12, 100, 64), (2, 6, 256, 64),
+                                     (1, 2, 513, 64), (1, 25, 70, 64), (2, 2, 65, 32), (1, 1, 1, 64),
+                                     (1, 2, 40, 128)])
+def test_attention(dtype, B, H, T, D):
+    q, k, v = (randn(B, H, T, D, seed=s).to(dtype) for s in (20, 21, 22))
+    y = cg.cutile_causal_attention(q.cuda(), k.cuda(), v.cuda(), H)
+    ref = R.causal_attention(q.double(), k.double(), v.double())
+    if dtype == torch.float32:
+        torch.testing.assert_close(y.cpu().double(), ref, atol=1e-3, rtol=1e-3)
+    else:
+        assert rel_err(y, ref) < BF16_REL
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_attention_from_fused_qkv_layout(dtype):
+    B, T, H, D = 2, 150, 12, 64
+    C = H * D
+    qkv = randn(B, T, 3 * C, seed=23).to(dtype).cuda()
+    q4 = qkv.view(B, T, 3, H, D)
+    out = torch.empty((B, T, C), dtype=dtype, device="cuda")
+    ops.attention_prefill(q4[:, :, 0].transpose(1, 2), q4[:, :, 1].transpose(1, 2), q4[:, :, 2].transpose(1, 2),
+                          out.view(B, T, H, D).transpose(1, 2))
+    qc = qkv.cpu().double().view(B, T, 3, H, D)
+    ref = R.causal_attention(*(qc[:, :, j].transpose(1, 2) for j in range(3))).transpose(1, 2).reshape(B, T, C)
+    if dtype == torch.float32:
+        torch.testing.assert_close(out.cpu().double(), ref, atol=1e-3, rtol=1e-3)
+    else:
+        assert rel_err(out, ref) < BF16_REL
+
+
+# ----------------------------------------------------------------- KV cache + decode
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,H,D,Tmax,Lq", [(4, 12, 64, 256, 200), (64, 12, 64, 256, 129), (2, 25, 64, 1024, 1000),
+                                           (3, 3, 16, 64, 5), (1, 2, 128, 300, 300), (8, 12, 64, 256, 256)])
+def test_kv_append_and_decode(dtype, B, H, D, Tmax, Lq):
+    C = H * D
+    cache_k = torch.zeros((B, H, Tmax, D), dtype=dtype, device="cuda")
+    cache_v = torch.zeros_like(cache_k)
+    qkv_prompt = randn(B, Lq - 1, 3 * C, seed=30).to(dtype).cuda()
+    ops.kv_append(qkv_prompt, cache_k, cache_v, pos0=0)
+    qkv_new = randn(B, 3 * C, seed=31).to(dtype).cuda()
+    pos = torch.tensor([Lq - 1], dtype=torch.int64, device="cuda")
+    ops.kv_append(qkv_new.view(B, 1, 3 * C), cache_k, cache_v, pos0=0, pos_dev=pos)
+    allqkv = torch.cat([qkv_prompt.cpu(), qkv_new.cpu().view(B, 1, 3 * C)], 1).double()
+    k_ref = allqkv[:, :, C:2 * C].view(B, Lq, H, D).transpose(1, 2)
+    v_ref = allqkv[:, :, 2 * C:].view(B, Lq, H, D).transpose(1, 2)
+    assert torch.equal(cache_k[:, :, :Lq].cpu().double(), k_ref)
+    assert torch.equal(cache_v[:, :, :Lq].cpu().double(), v_ref)
+    ws = torch.empty(max(16, ops.decode_workspace_bytes(B, H, D, Tmax)), dtype=torch.uint8, device="cuda")
+    out = torch.empty((B, C), dtype=dtype, device="cuda")
+    ops.attention_decode(qkv_new[:, :C], cache_k, cache_v, out, 1, ws, len_dev=pos)
+    q = qkv_new.cpu().double()[:, :C].view(B, H, 1, D)
+    att = torch.softmax((q @ k_ref.transpose(-1, -2)) / math.sqrt(D), dim=-1) @ v_ref
+    ref = att.view(B, C)
+    if dtype == torch.float32:
+        torch.testing.assert_close(out.cpu().double(), ref, atol=1e-4, rtol=1e-4)
+    else:
+        assert rel_err(out, ref) < BF16_REL
+    # host-length form agrees with the device-length form
+    out2 = torch.empty_like(out)
+    ws2 = torch.empty(max(16, ops.decode_workspace_bytes(B, H, D, Lq)), dtype=torch.uint8, device="cuda")
+    ops.attention_decode(qkv_new[:, :C], cache_k, cache_v, out2, Lq, ws2)
+    assert rel_err(out2, ref) < (1e-5 if dtype == torch.float32 else BF16_REL)
+
+
+# ----------------------------------------------------------------- argmax / advance
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_argmax_and_advance(dtype):
+    B, V = 5, 50257
+    logits = randn(B, V, seed=40).to(dtype)
+    logits[2, 17] = logits[2, 40000] = 100.0   # tie -> first index
+    big = torch.zeros((B, V + 3), dtype=dtype)
+    big[:, :V] = logits
+    tok = torch.empty(B, dtype=torch.int64, device="cuda")
+    ops.argmax(big.cuda()[:, :V], tok)
+    ref = logits.float().argmax(-1)
+    assert torch.equal(tok.cpu(), ref)
+    assert tok[2].item() == 17
+    seq = torch.zeros((B, 10), dtype=torch.int64, device="cuda")
+    pos = torch.tensor([3], dtype=torch.int64, device="cuda")
+    ops.decode_advance(tok, pos, seq)
+    assert pos.item() == 4
+    assert torch.equal(seq[:, 4].cpu(), ref)
