@@ -36,6 +36,7 @@ SIGNATURES = {
     "gpt_last_error_string": (ctypes.c_char_p, []),
     "gpt_device_error": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "gpt_sm_count": (_i32, []),
+    "gpt_launch_count": (_i64, []),
     "gpt_embedding": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i32, _p]),
     "gpt_embedding_pos": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _p]),
     "gpt_layernorm": (_i32, [_p, _p, _p, _p, _i64, _i64, _f32, _i32, _p]),

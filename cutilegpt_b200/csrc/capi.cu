@@ -8,6 +8,7 @@
 namespace gpt {
 
 static thread_local std::string t_last_error;
+static thread_local int64_t t_launches = 0;
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 
@@ -22,6 +23,7 @@ int fail(int status, const char* fmt, ...) {
 }
 
 int launch_status(const char* what) {
+  ++t_launches;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess)
     return fail(GPT_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
@@ -56,6 +58,8 @@ int gpt_version(void) { return 1; }
 const char* gpt_last_error_string(void) { return gpt::t_last_error.c_str(); }
 
 int gpt_sm_count(void) { return gpt::device_sm_count(); }
+
+int64_t gpt_launch_count(void) { return gpt::t_launches; }
 
 int gpt_device_error(int* code_out) {
   GPT_CHECK_ARG(code_out != nullptr, "gpt_device_error: null code_out");

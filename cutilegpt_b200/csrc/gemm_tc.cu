@@ -270,6 +270,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int row0 = m_blk * BM + quad * 32;
       for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
+        // lane == column in the store phase below.
+        const int col = n_blk * BN + c * 32 + lane;
+        const bool col_ok = col < p.N;
+        // Residual loads for all 32 rows are issued first so their latency
+        // overlaps the TMEM load and the shared-memory transpose.
+        float res[32];
+        if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+#pragma unroll
+          for (int rr = 0; rr < 32; ++rr) {
+            const int row = row0 + rr;
+            res[rr] = (row < p.M && col_ok) ? __bfloat162float(p.resid[(int64_t)row * p.ldr + col]) : 0.f;
+          }
+        }
+        float bcol = 0.f;
+        if (EPI != GPT_EPI_NONE && col_ok) bcol = __bfloat162float(p.bias[col]);
         uint32_t r[32];
         const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32);
         tmem_ld32(taddr, r);
@@ -278,17 +293,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 32; ++j) stg[lane * kStageRowPitch + j] = __uint_as_float(r[j]);
         __syncwarp();
         // lane == column: bias / GELU / residual, coalesced row stores.
-        const int col = n_blk * BN + c * 32 + lane;
-        const bool col_ok = col < p.N;
-        float bcol = 0.f;
-        if (EPI != GPT_EPI_NONE && col_ok) bcol = __bfloat162float(p.bias[col]);
-#pragma unroll 4
+#pragma unroll
         for (int rr = 0; rr < 32; ++rr) {
           const int row = row0 + rr;
           if (row < p.M && col_ok) {
             float v = stg[rr * kStageRowPitch + lane] + bcol;
             if (EPI == GPT_EPI_BIAS_GELU) v = gelu_tanh<true>(v);
-            if (EPI == GPT_EPI_BIAS_RESIDUAL) v += __bfloat162float(p.resid[(int64_t)row * p.ldr + col]);
+            if (EPI == GPT_EPI_BIAS_RESIDUAL) v += res[rr];
             p.C[(int64_t)row * p.ldc + col] = __float2bfloat16_rn(v);
           }
         }

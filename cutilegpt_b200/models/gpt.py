@@ -65,10 +65,10 @@ class _DecodeState:
         self.logits = torch.empty((B, cfg.vocab_size), dtype=dtype, device=device)
         self.tok = torch.empty((B,), dtype=torch.int64, device=device)
         self.pos = torch.zeros((1,), dtype=torch.int64, device=device)
+        self.seq = torch.empty((B, Tmax), dtype=torch.int64, device=device)
         nbytes = ops.decode_workspace_bytes(B, H, D, Tmax)
         self.dec_ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=device)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
-        self.graph_seq = None
 
 
 class CutileGPT:
@@ -85,6 +85,8 @@ class CutileGPT:
         self.weight_transposes: Dict[str, torch.Tensor] = {}
         self._ws: Dict[Tuple[int, int], _Workspace] = {}
         self._dec: Dict[Tuple[int, int], _DecodeState] = {}
+        # Optional object with start(flops) / stop() around every GEMM launch.
+        self.kernel_timer = None
         self._init_weights(seed)
 
     # ------------------------------------------------------------------ weights
@@ -139,6 +141,16 @@ class CutileGPT:
     def _w(self, key: str) -> torch.Tensor:
         return self.weights[key]
 
+    def _gemm(self, a, w, out, **kw):
+        """ops.gemm, bracketed by the optional kernel timer's CUDA events (used by bench.py)."""
+        t = self.kernel_timer
+        if t is None:
+            return ops.gemm(a, w, out, **kw)
+        t.start(2 * a.shape[0] * w.shape[0] * w.shape[1])
+        ops.gemm(a, w, out, **kw)
+        t.stop()
+        return out
+
     # ------------------------------------------------------------------ forward
     def __call__(self, idx) -> Tuple[torch.Tensor, None]:
         return self.forward(idx)
@@ -167,16 +179,16 @@ class CutileGPT:
         for i in range(cfg.n_layer):
             p = f'h.{i}.'
             ops.layernorm(ws.x, self._w(p + 'ln_1.weight'), self._w(p + 'ln_1.bias'), ws.h)
-            ops.gemm(ws.h, self._w(p + 'attn.c_attn.weight'), ws.qkv, bias=self._w(p + 'attn.c_attn.bias'))
+            self._gemm(ws.h, self._w(p + 'attn.c_attn.weight'), ws.qkv, bias=self._w(p + 'attn.c_attn.bias'))
             if cache is not None:
                 ops.kv_append(ws.qkv.view(B, T, 3 * C), cache[i, 0], cache[i, 1], pos0=0)
             ops.attention_prefill(q, k, v, att4, scale)
-            ops.gemm(ws.att, self._w(p + 'attn.c_proj.weight'), ws.x, bias=self._w(p + 'attn.c_proj.bias'),
+            self._gemm(ws.att, self._w(p + 'attn.c_proj.weight'), ws.x, bias=self._w(p + 'attn.c_proj.bias'),
                      resid=ws.x)
             ops.layernorm(ws.x, self._w(p + 'ln_2.weight'), self._w(p + 'ln_2.bias'), ws.h)
-            ops.gemm(ws.h, self._w(p + 'mlp.c_fc.weight'), ws.f, bias=self._w(p + 'mlp.c_fc.bias'),
+            self._gemm(ws.h, self._w(p + 'mlp.c_fc.weight'), ws.f, bias=self._w(p + 'mlp.c_fc.bias'),
                      epilogue=L.EPI_BIAS_GELU)
-            ops.gemm(ws.f, self._w(p + 'mlp.c_proj.weight'), ws.x, bias=self._w(p + 'mlp.c_proj.bias'),
+            self._gemm(ws.f, self._w(p + 'mlp.c_proj.weight'), ws.x, bias=self._w(p + 'mlp.c_proj.bias'),
                      resid=ws.x)
         ops.layernorm(ws.x, self._w('ln_f.weight'), self._w('ln_f.bias'), ws.h)
 
@@ -199,7 +211,7 @@ class CutileGPT:
             return logits, None
         ws = self._workspace(B, T)
         self._blocks(idx, ws)
-        ops.gemm(ws.h, self._w('lm_head.weight'), logits.view(B * T, cfg.vocab_size))
+        self._gemm(ws.h, self._w('lm_head.weight'), logits.view(B * T, cfg.vocab_size))
         return logits, None
 
     def forward_last(self, idx, out: Optional[torch.Tensor] = None,
@@ -213,7 +225,7 @@ class CutileGPT:
         if out is None:
             out = torch.empty((B, self.config.vocab_size), dtype=self.dtype, device=self.device)
         last = ws.h.view(B, T, -1)[:, T - 1, :]          # row-strided [B, C] view
-        ops.gemm(last, self._w('lm_head.weight'), out)
+        self._gemm(last, self._w('lm_head.weight'), out)
         return out
 
     # ------------------------------------------------------------------ decode
@@ -238,19 +250,19 @@ class CutileGPT:
         for i in range(cfg.n_layer):
             p = f'h.{i}.'
             ops.layernorm(st.x, self._w(p + 'ln_1.weight'), self._w(p + 'ln_1.bias'), st.h)
-            ops.gemm(st.h, self._w(p + 'attn.c_attn.weight'), st.qkv, bias=self._w(p + 'attn.c_attn.bias'))
+            self._gemm(st.h, self._w(p + 'attn.c_attn.weight'), st.qkv, bias=self._w(p + 'attn.c_attn.bias'))
             ops.kv_append(st.qkv.view(B, 1, 3 * C), st.cache[i, 0], st.cache[i, 1], pos0=0, pos_dev=st.pos)
             ops.attention_decode(q, st.cache[i, 0], st.cache[i, 1], st.att, 1, st.dec_ws, scale,
                                  len_dev=st.pos)
-            ops.gemm(st.att, self._w(p + 'attn.c_proj.weight'), st.x, bias=self._w(p + 'attn.c_proj.bias'),
+            self._gemm(st.att, self._w(p + 'attn.c_proj.weight'), st.x, bias=self._w(p + 'attn.c_proj.bias'),
                      resid=st.x)
             ops.layernorm(st.x, self._w(p + 'ln_2.weight'), self._w(p + 'ln_2.bias'), st.h)
-            ops.gemm(st.h, self._w(p + 'mlp.c_fc.weight'), st.f, bias=self._w(p + 'mlp.c_fc.bias'),
+            self._gemm(st.h, self._w(p + 'mlp.c_fc.weight'), st.f, bias=self._w(p + 'mlp.c_fc.bias'),
                      epilogue=L.EPI_BIAS_GELU)
-            ops.gemm(st.f, self._w(p + 'mlp.c_proj.weight'), st.x, bias=self._w(p + 'mlp.c_proj.bias'),
+            self._gemm(st.f, self._w(p + 'mlp.c_proj.weight'), st.x, bias=self._w(p + 'mlp.c_proj.bias'),
                      resid=st.x)
         ops.layernorm(st.x, self._w('ln_f.weight'), self._w('ln_f.bias'), st.h)
-        ops.gemm(st.h, self._w('lm_head.weight'), st.logits)
+        self._gemm(st.h, self._w('lm_head.weight'), st.logits)
 
     def _greedy_step(self, st: _DecodeState, seq: torch.Tensor) -> None:
         self._decode_step(st)
@@ -286,9 +298,9 @@ class CutileGPT:
         greedy = top_k == 1
         if not use_kv_cache or total > cfg.block_size:
             return self._generate_reforward(idx, max_new_tokens, temperature, top_k, generator)
-        seq = torch.empty((B, total), dtype=torch.int64, device=self.device)
-        seq[:, :T0] = idx
         st = self._decode_state(B, total)
+        seq = st.seq
+        seq[:, :T0] = idx
         # prefill: K/V of the prompt into the cache, logits of the last position
         self.forward_last(idx, out=st.logits, cache=st.cache)
         if greedy:
@@ -298,36 +310,33 @@ class CutileGPT:
         seq[:, T0] = st.tok
         st.pos.fill_(T0)
         steps = max_new_tokens - 1
-        if steps == 0:
-            return seq
         if not greedy:
             for _ in range(steps):
                 self._decode_step(st)
                 st.tok.copy_(self._sample(st.logits, temperature, top_k, generator))
                 ops.decode_advance(st.tok, st.pos, seq)
-            return seq
-        if not use_cuda_graph or steps < 3:
+        elif not use_cuda_graph or steps < 2:
             for _ in range(steps):
                 self._greedy_step(st, seq)
-            return seq
-        # First step eagerly (warms every kernel), then capture one step and replay.
-        self._greedy_step(st, seq)
-        self._capture(st, seq)
-        for _ in range(steps - 1):
-            st.graph.replay()
-        return seq
+        else:
+            if st.graph is None:
+                # one eager step warms every kernel, then the step is captured once per state
+                self._greedy_step(st, seq)
+                steps -= 1
+                self._capture(st)
+            for _ in range(steps):
+                st.graph.replay()
+        return seq.clone()
 
-    def _capture(self, st: _DecodeState, seq: torch.Tensor) -> None:
-        if st.graph is not None and st.graph_seq is seq:
-            return
+    def _capture(self, st: _DecodeState) -> None:
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self._greedy_step(st, seq)
+                self._greedy_step(st, st.seq)
         torch.cuda.current_stream(self.device).wait_stream(s)
-        st.graph, st.graph_seq = g, seq
+        st.graph = g
 
     def _generate_reforward(self, idx, max_new_tokens, temperature, top_k, generator) -> torch.Tensor:
         """Reference semantics without a cache: re-run the (cropped) prefix each step."""

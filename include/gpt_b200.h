@@ -58,6 +58,8 @@ GPT_API const char* gpt_last_error_string(void);
 GPT_API int gpt_device_error(int* code_out);
 /* Number of SMs of the current device (0 if no device). */
 GPT_API int gpt_sm_count(void);
+/* Kernels this thread has launched through the library so far. */
+GPT_API int64_t gpt_launch_count(void);
 
 /* ---- embedding --------------------------------------------------------- */
 /* out[i, :] = weight[idx[i], :] for i < n_idx.  Indices outside [0, vocab)
