@@ -157,6 +157,47 @@ def barrier(world):
 
 
 # --------------------------------------------------------------------------- ours
+def run_decode(args, model, cfg, rank, world, dev):
+    """batch 64 sharded over the ranks, prompt 128, 128 greedy KV-cache steps."""
+    from cutilegpt_b200.distributed import shard_range
+    Bg, P, S = 64, 128, 128
+    lo, hi = shard_range(Bg, rank, world)
+    g2 = torch.Generator().manual_seed(77)
+    prompt = torch.randint(0, cfg.vocab_size, (Bg, P), generator=g2)[lo:hi].to(dev)
+    model.generate(prompt, S, top_k=1)                 # warm-up; captures the decode-step graph
+    barrier(world)
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    model.generate(prompt, 1, top_k=1)                 # prefill + first token
+    p1.record()
+    d0.record()
+    model.generate(prompt, S, top_k=1)                 # prefill + S-1 graph-replayed decode steps
+    d1.record()
+    barrier(world)
+    gen_ms = max_over_ranks(d0.elapsed_time(d1), world)
+    pre_ms = max_over_ranks(p0.elapsed_time(p1), world)
+    dec_steps = S - 1
+    dec_ms = max(gen_ms - pre_ms, 1e-6)
+    dec_tok_s = Bg * dec_steps / (dec_ms / 1e3)
+    # HBM bytes per decode step on one rank: weights once + KV read (mean length) + KV write + logits
+    Bl = hi - lo
+    wbytes = sum(t.numel() * t.element_size() for k, t in model.weights.items() if k != "lm_head.weight")
+    C, Lyr = cfg.n_embd, cfg.n_layer
+    mean_len = P + 1 + (dec_steps - 1) / 2
+    step_bytes = (wbytes + Bl * Lyr * 2 * C * 2 * mean_len + Bl * Lyr * 2 * C * 2
+                  + Bl * cfg.vocab_size * 2)
+    _, peak_gbs, src = load_peaks()
+    step_s = dec_ms / dec_steps / 1e3
+    dec = {"value": dec_tok_s, "unit": "tokens/s", "batch": Bg, "prompt": P, "steps": S,
+           "ms_per_step": dec_ms / dec_steps, "prefill_ms": pre_ms,
+           "hbm_roofline": {"achieved": step_bytes / step_s / 1e9, "peak": peak_gbs, "unit": "GB/s",
+                            "frac": step_bytes / step_s / 1e9 / peak_gbs,
+                            "bytes_per_step_per_gpu": step_bytes, "peak_source": src},
+           "scaling": "strong", "cuda_graph": True}
+    return dec
+
+
 def run_ours(args, rank, world, local):
     from cutilegpt_b200 import CutileGPT, GPTConfig, _lib
     from cutilegpt_b200.distributed import shard_range
@@ -166,6 +207,8 @@ def run_ours(args, rank, world, local):
     cfg = GPTConfig.gpt2()
     B, T = args.batch, args.seq
     model = CutileGPT(cfg, dtype=torch.bfloat16, device=dev, seed=1234)   # same weights on every rank
+    if args.decode_only:
+        return {"dec": run_decode(args, model, cfg, rank, world, dev)}
     gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
     idx_host = torch.randint(0, cfg.vocab_size, (B, T), generator=gen).pin_memory()
     idx = idx_host.to(dev)
@@ -224,45 +267,7 @@ def run_ours(args, rank, world, local):
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
     e2e_value = tokens / (e2e_ms / 1e3)
     torch.cuda.empty_cache()
-
-    # ---- decode: batch 64 sharded over the ranks
-    dec = None
-    if not args.no_decode:
-        Bg, P, S = 64, 128, 128
-        lo, hi = shard_range(Bg, rank, world)
-        g2 = torch.Generator().manual_seed(77)
-        prompt = torch.randint(0, cfg.vocab_size, (Bg, P), generator=g2)[lo:hi].to(dev)
-        model.generate(prompt, S, top_k=1)                 # warm-up; captures the decode-step graph
-        barrier(world)
-        p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        p0.record()
-        model.generate(prompt, 1, top_k=1)                 # prefill + first token
-        p1.record()
-        d0.record()
-        model.generate(prompt, S, top_k=1)                 # prefill + S-1 graph-replayed decode steps
-        d1.record()
-        barrier(world)
-        gen_ms = max_over_ranks(d0.elapsed_time(d1), world)
-        pre_ms = max_over_ranks(p0.elapsed_time(p1), world)
-        dec_steps = S - 1
-        dec_ms = max(gen_ms - pre_ms, 1e-6)
-        dec_tok_s = Bg * dec_steps / (dec_ms / 1e3)
-        # HBM bytes per decode step on one rank: weights once + KV read (mean length) + KV write + logits
-        Bl = hi - lo
-        wbytes = sum(t.numel() * t.element_size() for k, t in model.weights.items() if k != "lm_head.weight")
-        C, Lyr = cfg.n_embd, cfg.n_layer
-        mean_len = P + 1 + (dec_steps - 1) / 2
-        step_bytes = (wbytes + Bl * Lyr * 2 * C * 2 * mean_len + Bl * Lyr * 2 * C * 2
-                      + Bl * cfg.vocab_size * 2)
-        _, peak_gbs, src = load_peaks()
-        step_s = dec_ms / dec_steps / 1e3
-        dec = {"value": dec_tok_s, "unit": "tokens/s", "batch": Bg, "prompt": P, "steps": S,
-               "ms_per_step": dec_ms / dec_steps, "prefill_ms": pre_ms,
-               "hbm_roofline": {"achieved": step_bytes / step_s / 1e9, "peak": peak_gbs, "unit": "GB/s",
-                                "frac": step_bytes / step_s / 1e9 / peak_gbs,
-                                "bytes_per_step_per_gpu": step_bytes, "peak_source": src},
-               "scaling": "strong", "cuda_graph": True}
+    dec = None if args.no_decode else run_decode(args, model, cfg, rank, world, dev)
     return dict(value=value, ms=ms_max / args.steps, tokens=tokens, launches=launches, clk=clk,
                 gemm_ms=gemm_ms, gemm_launches=gemm_launches, gemm_flops=gemm_flops, e2e_value=e2e_value,
                 e2e_h2d=B * T * 8, e2e_d2h=B * cfg.vocab_size * 2, dec=dec, cfg=cfg)
@@ -333,6 +338,7 @@ def main():
     ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--decode-only", action="store_true", help="only the config-4 decode run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -343,6 +349,12 @@ def main():
     from cutilegpt_b200.distributed import init_from_env
     rank, world, local = init_from_env("nccl" if world_env > 1 else None)
     r = run_ours(args, rank, world, local)
+    if args.decode_only:
+        if rank == 0:
+            print(json.dumps({"decode": r["dec"]}), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, n = cpu_sample(args.seq)
