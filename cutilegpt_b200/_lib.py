@@ -48,6 +48,8 @@ SIGNATURES = {
     "gpt_attention_decode_workspace_size": (_i64, [_i64, _i64, _i64, _i64]),
     "gpt_attention_decode": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p,
                                     _f32, _p, _i32, _p]),
+    "gpt_attention_decode_noalloc": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p,
+                                            _f32, _i32, _p]),
     "gpt_decode_advance": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p]),
     "gpt_argmax": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
 }

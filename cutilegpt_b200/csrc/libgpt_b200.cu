@@ -5,3 +5,4 @@
 #include "gemm_simt.cu"
 #include "attention.cu"
 #include "decode.cu"
+#include "decode_noalloc.cu"

@@ -149,6 +149,25 @@ GPT_API int gpt_attention_decode(const void* q, int64_t ld_q, const void* k_cach
                          int64_t L, const int64_t* len_dev, float scale,
                          void* workspace, int dtype, void* stream);
 
+/* Same computation as gpt_attention_decode, for callers that cannot
+ * allocate device memory (fixed-arena runtimes, plugins barred from calling
+ * cudaMalloc after start-up, latency-critical loops that must not enter the
+ * driver's allocator). No counterpart in the reference, which has no decode
+ * path. Instead of a caller workspace, the split-KV partials go to a fixed
+ * GPT_NOALLOC_DECODE_SCRATCH_BYTES array inside the library (one per GPU,
+ * held from library load until exit); sizes whose
+ * gpt_attention_decode_workspace_size exceeds it return GPT_ERR_SHAPE. The
+ * first call on a device looks up that array's device address, so make it
+ * before any stream capture on that device. All calls on a device share the
+ * array: calls whose kernels may overlap on the GPU race on it. Nothing in
+ * it needs clearing between calls. Allocates nothing. */
+#define GPT_NOALLOC_DECODE_SCRATCH_BYTES (256 * 1024)
+GPT_API int gpt_attention_decode_noalloc(const void* q, int64_t ld_q,
+                         const void* k_cache, const void* v_cache, void* out,
+                         int64_t ld_out, int64_t B, int64_t H, int64_t D,
+                         int64_t Tmax, int64_t L, const int64_t* len_dev,
+                         float scale, int dtype, void* stream);
+
 /* End of a decode step: seq[b, *pos_dev + 1] = tok[b] for b < B (seq row
  * stride ld_seq, skipped when seq is NULL), then *pos_dev += 1. Positions
  * at or past seq_len are not written. One tiny kernel. */
