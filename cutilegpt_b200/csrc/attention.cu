@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const T* __restrict__ q,
                                                         const T* __restrict__ v, T* __restrict__ o,
                                                         Strides qs, Strides ks, Strides vs, Strides os,
                                                         int H, int T_, int D, float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float Ks[TN][DM];
   __shared__ float Vs[TN][DM];
   const int bh = blockIdx.y, b = bh / H, h = bh % H;
@@ -135,6 +137,8 @@ __global__ void __launch_bounds__(128) attn_mma_kernel(const __nv_bfloat16* __re
                                                        __nv_bfloat16* __restrict__ o, Strides qs,
                                                        Strides ks, Strides vs, Strides os, int H, int T_,
                                                        float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ __align__(128) uint8_t sQ[kBM * kD * 2];
   __shared__ __align__(128) uint8_t sK[2][kBN * kD * 2];
   __shared__ __align__(128) uint8_t sV[2][kBN * kD * 2];
@@ -307,13 +311,13 @@ static int launch_simt(const void* q, const void* k, const void* v, void* o, Str
   const T *qq = (const T*)q, *kk = (const T*)k, *vv = (const T*)v;
   T* oo = (T*)o;
   if (D <= 16)
-    attn_simt_kernel<T, 16, 32><<<grid, 128, 0, st>>>(qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
+    launch_pdl(attn_simt_kernel<T, 16, 32>, dim3(grid), dim3(128), 0, st, qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
   else if (D <= 32)
-    attn_simt_kernel<T, 32, 32><<<grid, 128, 0, st>>>(qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
+    launch_pdl(attn_simt_kernel<T, 32, 32>, dim3(grid), dim3(128), 0, st, qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
   else if (D <= 64)
-    attn_simt_kernel<T, 64, 16><<<grid, 128, 0, st>>>(qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
+    launch_pdl(attn_simt_kernel<T, 64, 16>, dim3(grid), dim3(128), 0, st, qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
   else
-    attn_simt_kernel<T, 128, 8><<<grid, 128, 0, st>>>(qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
+    launch_pdl(attn_simt_kernel<T, 128, 8>, dim3(grid), dim3(128), 0, st, qq, kk, vv, oo, qs, ks, vs, os, (int)H, (int)T_, (int)D, sl2);
   return launch_status("attention_simt");
 }
 
@@ -343,7 +347,7 @@ extern "C" int gpt_attention_prefill(const void* q, const void* k, const void* v
     if (D == 64 && al(q, qs.b, qs.h, qs.t) && al(k, ks.b, ks.h, ks.t) && al(v, vs.b, vs.h, vs.t) &&
         gpt::aligned(out, 4) && os.b % 2 == 0 && os.h % 2 == 0 && os.t % 2 == 0) {
       dim3 grid((unsigned)((T + kBM - 1) / kBM), (unsigned)(B * H));
-      attn_mma_kernel<<<grid, 128, 0, st>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)k,
+      gpt::launch_pdl(attn_mma_kernel, dim3(grid), dim3(128), 0, st, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k,
                                             (const __nv_bfloat16*)v, (__nv_bfloat16*)out, qs, ks, vs, os,
                                             (int)H, (int)T, sl2);
       return gpt::launch_status("attention_mma");

@@ -9,6 +9,9 @@ namespace gpt {
 
 static thread_local std::string t_last_error;
 static thread_local int64_t t_launches = 0;
+static thread_local cudaError_t t_launch_error = cudaSuccess;
+
+void note_launch_error(cudaError_t e) { t_launch_error = e; }
 
 void set_error(const std::string& msg) { t_last_error = msg; }
 
@@ -24,7 +27,10 @@ int fail(int status, const char* fmt, ...) {
 
 int launch_status(const char* what) {
   ++t_launches;
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = t_launch_error;
+  t_launch_error = cudaSuccess;
+  cudaError_t last = cudaGetLastError();
+  if (e == cudaSuccess) e = last;
   if (e != cudaSuccess)
     return fail(GPT_ERR_CUDA, "%s: launch failed: %s", what, cudaGetErrorString(e));
   return GPT_OK;

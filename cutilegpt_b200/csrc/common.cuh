@@ -8,6 +8,7 @@
 #include <stdint.h>
 #include <stdio.h>
 #include <string>
+#include <utility>
 
 #include "../../include/gpt_b200.h"
 
@@ -37,6 +38,33 @@ int fail(int status, const char* fmt, ...);
 
 // Checks the launch that was just issued; returns GPT_OK or GPT_ERR_CUDA.
 int launch_status(const char* what);
+// Records a launch error returned by cudaLaunchKernelEx for launch_status().
+void note_launch_error(cudaError_t e);
+
+// Programmatic dependent launch: every kernel of this library is launched
+// with programmatic stream serialisation, so its CTAs may start (set up
+// barriers, TMEM, prefetch weights) while the previous kernel in the stream
+// is still running. Each kernel calls pdl_wait() before it reads anything a
+// predecessor may write or writes anything a predecessor may read, and
+// pdl_trigger() once its own CTAs no longer need to hold back the next
+// kernel. The next kernel's CTAs start only after every CTA of this grid has
+// started, so early triggering cannot starve this grid's later waves.
+template <typename... KArgs, typename... Args>
+inline void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) note_launch_error(e);
+}
 
 inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
@@ -95,6 +123,9 @@ __device__ __forceinline__ float warp_max(float v) {
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t global_timer_ns() {
   uint64_t t;

@@ -37,6 +37,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict
                                                              int64_t ld_out, int H, int64_t Tmax, int L0,
                                                              const int64_t* __restrict__ len_dev,
                                                              float scale_log2, float* __restrict__ ws) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = 16 / sizeof(T);   // elements per lane vector
   constexpr int LPK = D / V;          // lanes per key
   constexpr int KPW = 32 / LPK;       // keys per warp iteration
@@ -159,6 +161,8 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict
 template <typename T, int D>
 __global__ void combine_kernel(const float* __restrict__ ws, int nsplit, T* __restrict__ out, int64_t ld_out,
                                int H) {
+  pdl_wait();
+  pdl_trigger();
   const int bh = blockIdx.x, b = bh / H, h = bh % H;
   const int d = threadIdx.x;
   const float* part = ws + (int64_t)bh * nsplit * (D + 2);
@@ -182,11 +186,11 @@ static int launch(const void* q, int64_t ld_q, const void* kc, const void* vc, v
   if (sms <= 0) sms = 148;
   int ns = num_splits(B, H, len_dev ? Tmax : L, sms);
   dim3 grid((unsigned)ns, (unsigned)(B * H));
-  decode_kernel<T, D><<<grid, kWarps * 32, 0, st>>>((const T*)q, ld_q, (const T*)kc, (const T*)vc, (T*)out,
+  launch_pdl(decode_kernel<T, D>, dim3(grid), dim3(kWarps * 32), 0, st, (const T*)q, ld_q, (const T*)kc, (const T*)vc, (T*)out,
                                                     ld_out, (int)H, Tmax, (int)L, len_dev, sl2, (float*)ws);
   int s = launch_status("attention_decode");
   if (s || ns == 1) return s;
-  combine_kernel<T, D><<<(unsigned)(B * H), D, 0, st>>>((const float*)ws, ns, (T*)out, ld_out, (int)H);
+  launch_pdl(combine_kernel<T, D>, dim3((unsigned)(B * H)), dim3(D), 0, st, (const float*)ws, ns, (T*)out, ld_out, (int)H);
   return launch_status("attention_decode_combine");
 }
 

@@ -38,6 +38,8 @@ __global__ void embedding_kernel(const int64_t* __restrict__ idx, int64_t n_tok,
                                  int64_t vocab, int64_t n_pos, int64_t C, int64_t T_,
                                  int64_t pos0, const int64_t* __restrict__ pos_dev,
                                  T* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   int warps = blockDim.x >> 5;
   int64_t tok = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
@@ -87,11 +89,11 @@ static int launch_embedding(const int64_t* idx, int64_t n_tok, const void* wte, 
   const T* b = (const T*)wpe;
   T* o = (T*)out;
   if (wpe) {
-    if (vec) embedding_kernel<T, true, true><<<grid, warps * 32, 0, st>>>(idx, n_tok, a, b, vocab, n_pos, C, T_, pos0, pos_dev, o);
-    else embedding_kernel<T, true, false><<<grid, warps * 32, 0, st>>>(idx, n_tok, a, b, vocab, n_pos, C, T_, pos0, pos_dev, o);
+    if (vec) launch_pdl(embedding_kernel<T, true, true>, dim3(grid), dim3(warps * 32), 0, st, idx, n_tok, a, b, vocab, n_pos, C, T_, pos0, pos_dev, o);
+    else launch_pdl(embedding_kernel<T, true, false>, dim3(grid), dim3(warps * 32), 0, st, idx, n_tok, a, b, vocab, n_pos, C, T_, pos0, pos_dev, o);
   } else {
-    if (vec) embedding_kernel<T, false, true><<<grid, warps * 32, 0, st>>>(idx, n_tok, a, b, vocab, n_pos, C, 1, 0, nullptr, o);
-    else embedding_kernel<T, false, false><<<grid, warps * 32, 0, st>>>(idx, n_tok, a, b, vocab, n_pos, C, 1, 0, nullptr, o);
+    if (vec) launch_pdl(embedding_kernel<T, false, true>, dim3(grid), dim3(warps * 32), 0, st, idx, n_tok, a, b, vocab, n_pos, C, 1, 0, nullptr, o);
+    else launch_pdl(embedding_kernel<T, false, false>, dim3(grid), dim3(warps * 32), 0, st, idx, n_tok, a, b, vocab, n_pos, C, 1, 0, nullptr, o);
   }
   return launch_status("embedding");
 }
@@ -110,6 +112,8 @@ __global__ void __launch_bounds__(128) layernorm_vec_kernel(const T* __restrict_
                                                             const T* __restrict__ w,
                                                             const T* __restrict__ b, T* y,
                                                             int64_t M, int C, float eps) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = Vec16<T>::N;
   int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
@@ -162,6 +166,8 @@ __global__ void __launch_bounds__(128) layernorm_generic_kernel(const T* __restr
                                                                 const T* __restrict__ w,
                                                                 const T* __restrict__ b, T* y,
                                                                 int64_t M, int C, float eps) {
+  pdl_wait();
+  pdl_trigger();
   int64_t row = (int64_t)blockIdx.x * 4 + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -194,14 +200,14 @@ static int launch_layernorm(const void* x, const void* w, const void* b, void* y
   if (vec && nv <= 8) {
     switch (nv) {
 #define GPT_LN_CASE(n) \
-  case n: layernorm_vec_kernel<T, n><<<grid, 128, 0, st>>>(xp, wp, bp, yp, M, (int)C, eps); break;
+  case n: launch_pdl(layernorm_vec_kernel<T, n>, dim3(grid), dim3(128), 0, st, xp, wp, bp, yp, M, (int)C, eps); break;
       GPT_LN_CASE(1) GPT_LN_CASE(2) GPT_LN_CASE(3) GPT_LN_CASE(4)
       GPT_LN_CASE(5) GPT_LN_CASE(6) GPT_LN_CASE(7) GPT_LN_CASE(8)
 #undef GPT_LN_CASE
       default: break;
     }
   } else {
-    layernorm_generic_kernel<T><<<grid, 128, 0, st>>>(xp, wp, bp, yp, M, (int)C, eps);
+    launch_pdl(layernorm_generic_kernel<T>, dim3(grid), dim3(128), 0, st, xp, wp, bp, yp, M, (int)C, eps);
   }
   return launch_status("layernorm");
 }
@@ -213,6 +219,8 @@ static int launch_layernorm(const void* x, const void* w, const void* b, void* y
 // ============================================================================
 template <typename T, bool kFast>
 __global__ void __launch_bounds__(256) gelu_kernel(const T* x, T* y, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = Vec16<T>::N;
   int64_t nvec = n / V;
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
@@ -229,6 +237,8 @@ __global__ void __launch_bounds__(256) gelu_kernel(const T* x, T* y, int64_t n) 
 
 template <typename T, bool kFast>
 __global__ void __launch_bounds__(256) gelu_scalar_kernel(const T* x, T* y, int64_t n) {
+  pdl_wait();
+  pdl_trigger();
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
     y[i] = Tr<T>::from_f(gelu_tanh<kFast>(Tr<T>::to_f(x[i])));
@@ -245,9 +255,9 @@ static int launch_gelu(const void* x, void* y, int64_t n, cudaStream_t st) {
   if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   if (aligned(x, 16) && aligned(y, 16))
-    gelu_kernel<T, kFast><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)y, n);
+    launch_pdl(gelu_kernel<T, kFast>, dim3((unsigned)blocks), dim3(256), 0, st, (const T*)x, (T*)y, n);
   else
-    gelu_scalar_kernel<T, kFast><<<(unsigned)blocks, 256, 0, st>>>((const T*)x, (T*)y, n);
+    launch_pdl(gelu_scalar_kernel<T, kFast>, dim3((unsigned)blocks), dim3(256), 0, st, (const T*)x, (T*)y, n);
   return launch_status("gelu");
 }
 
@@ -259,6 +269,8 @@ template <typename T>
 __global__ void kv_append_kernel(const T* __restrict__ qkv, int64_t ld, T* __restrict__ kc,
                                  T* __restrict__ vc, int64_t B, int64_t H, int64_t Tn, int64_t D,
                                  int64_t Tmax, int64_t pos0, const int64_t* __restrict__ pos_dev) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int V = Vec16<T>::N;
   int64_t C = H * D;
   if (pos_dev) pos0 += *pos_dev;
@@ -287,6 +299,8 @@ __global__ void kv_append_kernel(const T* __restrict__ qkv, int64_t ld, T* __res
 template <typename T>
 __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logits, int64_t ld,
                                                      int64_t V, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const T* row = logits + (int64_t)blockIdx.x * ld;
   float best = -INFINITY;
   int64_t bi = V;  // sentinel larger than any index
@@ -327,6 +341,8 @@ __global__ void __launch_bounds__(256) argmax_kernel(const T* __restrict__ logit
 // thread 0 bumps it.
 __global__ void decode_advance_kernel(const int64_t* __restrict__ tok, int64_t B, int64_t* seq,
                                       int64_t ld_seq, int64_t seq_len, int64_t* pos) {
+  pdl_wait();
+  pdl_trigger();
   const int64_t col = *pos + 1;
   if (seq && col >= 0 && col < seq_len)
     for (int64_t b = threadIdx.x; b < B; b += blockDim.x) seq[b * ld_seq + col] = tok[b];
@@ -412,10 +428,10 @@ int gpt_kv_append(const void* qkv, int64_t ld_qkv, void* k_cache, void* v_cache,
   int64_t blocks = (vecs + 255) / 256;
   if (blocks > 65535) blocks = 65535;
   if (dtype == GPT_F32)
-    gpt::kv_append_kernel<float><<<(unsigned)blocks, 256, 0, st>>>(
+    gpt::launch_pdl(gpt::kv_append_kernel<float>, dim3((unsigned)blocks), dim3(256), 0, st, 
         (const float*)qkv, ld_qkv, (float*)k_cache, (float*)v_cache, B, H, Tn, D, Tmax, pos0, pos_dev);
   else
-    gpt::kv_append_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
+    gpt::launch_pdl(gpt::kv_append_kernel<__nv_bfloat16>, dim3((unsigned)blocks), dim3(256), 0, st, 
         (const __nv_bfloat16*)qkv, ld_qkv, (__nv_bfloat16*)k_cache, (__nv_bfloat16*)v_cache, B, H, Tn,
         D, Tmax, pos0, pos_dev);
   return gpt::launch_status("kv_append");
@@ -429,9 +445,9 @@ int gpt_argmax(const void* logits, int64_t ld, int64_t B, int64_t V, int64_t* ou
   GPT_CHECK_ARG(logits && out, "gpt_argmax: null pointer");
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == GPT_F32)
-    gpt::argmax_kernel<float><<<(unsigned)B, 256, 0, st>>>((const float*)logits, ld, V, out);
+    gpt::launch_pdl(gpt::argmax_kernel<float>, dim3((unsigned)B), dim3(256), 0, st, (const float*)logits, ld, V, out);
   else
-    gpt::argmax_kernel<__nv_bfloat16><<<(unsigned)B, 256, 0, st>>>((const __nv_bfloat16*)logits, ld, V, out);
+    gpt::launch_pdl(gpt::argmax_kernel<__nv_bfloat16>, dim3((unsigned)B), dim3(256), 0, st, (const __nv_bfloat16*)logits, ld, V, out);
   return gpt::launch_status("argmax");
 }
 
@@ -439,7 +455,7 @@ int gpt_decode_advance(const int64_t* tok, int64_t B, int64_t* seq, int64_t ld_s
                        int64_t* pos_dev, void* stream) {
   GPT_CHECK_SHAPE(B >= 0 && (!seq || (ld_seq >= seq_len && seq_len >= 0)), "gpt_decode_advance: bad sizes");
   GPT_CHECK_ARG(pos_dev && (B == 0 || tok), "gpt_decode_advance: null pointer");
-  gpt::decode_advance_kernel<<<1, 256, 0, (cudaStream_t)stream>>>(tok, B, seq, ld_seq, seq_len, pos_dev);
+  gpt::launch_pdl(gpt::decode_advance_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream, tok, B, seq, ld_seq, seq_len, pos_dev);
   return gpt::launch_status("decode_advance");
 }
 

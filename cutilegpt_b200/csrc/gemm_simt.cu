@@ -20,6 +20,8 @@ __global__ void __launch_bounds__(kThreads) gemm_simt_kernel(const T* __restrict
                                                              const T* __restrict__ bias,
                                                              const T* R, int64_t ldr, T* C,
                                                              int64_t ldc, int M, int N, int K) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float As[2][BK][BM + 4];
   __shared__ float Ws[2][BK][BN + 4];
   const int tid = threadIdx.x;
@@ -102,16 +104,16 @@ int gemm(const void* A, int64_t lda, const void* W, const void* bias, const void
   T* c = (T*)C;
   switch (epi) {
     case GPT_EPI_NONE:
-      gemm_simt_kernel<T, GPT_EPI_NONE><<<grid, kThreads, 0, st>>>(a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
+      launch_pdl(gemm_simt_kernel<T, GPT_EPI_NONE>, dim3(grid), dim3(kThreads), 0, st, a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
       break;
     case GPT_EPI_BIAS:
-      gemm_simt_kernel<T, GPT_EPI_BIAS><<<grid, kThreads, 0, st>>>(a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
+      launch_pdl(gemm_simt_kernel<T, GPT_EPI_BIAS>, dim3(grid), dim3(kThreads), 0, st, a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
       break;
     case GPT_EPI_BIAS_GELU:
-      gemm_simt_kernel<T, GPT_EPI_BIAS_GELU><<<grid, kThreads, 0, st>>>(a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
+      launch_pdl(gemm_simt_kernel<T, GPT_EPI_BIAS_GELU>, dim3(grid), dim3(kThreads), 0, st, a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
       break;
     default:
-      gemm_simt_kernel<T, GPT_EPI_BIAS_RESIDUAL><<<grid, kThreads, 0, st>>>(a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
+      launch_pdl(gemm_simt_kernel<T, GPT_EPI_BIAS_RESIDUAL>, dim3(grid), dim3(kThreads), 0, st, a, lda, w, b, r, ldr, c, ldc, (int)M, (int)N, (int)K);
       break;
   }
   return launch_status("gemm_simt");
@@ -137,8 +139,11 @@ extern "C" int gpt_gemm(const void* A, int64_t lda, const void* W, const void* b
   GPT_CHECK_SHAPE(K > 0, "gpt_gemm: K must be positive");
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == GPT_BF16) {
-    if (gpt::tc::tc_eligible(A, lda, W, K, M, N))
+    if (gpt::tc::tc_eligible(A, lda, W, K, M, N)) {
+      if (M <= gpt::tc::kSkMaxM)
+        return gpt::tc::gemm_skinny(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
       return gpt::tc::gemm_bf16(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
+    }
     return gpt::simt::gemm<__nv_bfloat16>(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
   }
   return gpt::simt::gemm<float>(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);

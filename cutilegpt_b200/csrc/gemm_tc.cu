@@ -22,6 +22,7 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <stdlib.h>
 
 #include "common.cuh"
 
@@ -90,6 +91,26 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
       : "memory");
 }
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t pack2_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// 32 consecutive bf16 values starting at p (16-byte aligned) -> floats.
+__device__ __forceinline__ void load32_bf16(const __nv_bfloat16* p, float* out) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 raw = *reinterpret_cast<const uint4*>(p + 8 * i);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) out[8 * i + j] = __bfloat162float(e[j]);
+  }
+}
 __device__ __forceinline__ void tc_fence_before() {
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
 }
@@ -154,10 +175,10 @@ struct Smem {
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
 };
 
-template <int BN, int EPI>
+template <int BN, int EPI, bool kTmaStore>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const Params p) {
+                   const __grid_constant__ CUtensorMap tmC, const Params p) {
   using S = Smem<BN>;
   constexpr int kStages = S::kStages;
   extern __shared__ uint8_t smem_dyn[];
@@ -202,6 +223,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // Everything above touched only this CTA's resources; from here on the
+  // kernel reads activations and writes outputs of the stream.
+  pdl_wait();
+  pdl_trigger();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -253,8 +278,89 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
+  } else if constexpr (kTmaStore) {
+    // ------------------------------------------------------------ epilogue (TMA store)
+    // lane == row: 32 accumulator columns from TMEM, bias / GELU / residual in
+    // registers, packed bf16 into a 32x32 staging tile (64B-swizzled rows),
+    // written by one TMA bulk store per chunk. Two staging tiles per warp so
+    // the next chunk's math overlaps the previous store.
+    const int ew = warp - 2;
+    const int quad = warp & 3;
+    const int half = ew >> 2;
+    uint8_t* stg = reinterpret_cast<uint8_t*>(epi) + ew * 4096;
+    constexpr int kChunksPerHalf = BN / 64;
+    int sb = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
+      const int m_blk = tile % p.num_m;
+      const int n_blk = tile / p.num_m;
+      if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
+      tc_fence_after();
+      const int row0 = m_blk * BM + quad * 32;
+      const int row = row0 + lane;
+      const bool row_ok = row < p.M;
+      for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
+        const int col0 = n_blk * BN + c * 32;
+        const bool full = col0 + 32 <= p.N;
+        float badd[32], radd[32];
+        if (EPI != GPT_EPI_NONE) {
+          if (full) {
+            load32_bf16(p.bias + col0, badd);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) badd[j] = col0 + j < p.N ? __bfloat162float(p.bias[col0 + j]) : 0.f;
+          }
+        }
+        if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+          const __nv_bfloat16* rp = p.resid + (int64_t)row * p.ldr + col0;
+          if (row_ok && full) {
+            load32_bf16(rp, radd);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) radd[j] = (row_ok && col0 + j < p.N) ? __bfloat162float(rp[j]) : 0.f;
+          }
+        }
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+        uint32_t pk[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
+          if (EPI != GPT_EPI_NONE) { v0 += badd[2 * j]; v1 += badd[2 * j + 1]; }
+          if (EPI == GPT_EPI_BIAS_GELU) { v0 = gelu_tanh<true>(v0); v1 = gelu_tanh<true>(v1); }
+          if (EPI == GPT_EPI_BIAS_RESIDUAL) { v0 += radd[2 * j]; v1 += radd[2 * j + 1]; }
+          pk[j] = pack2_bf16(v0, v1);
+        }
+        // The store issued from this staging tile two chunks ago must have read it.
+        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+        __syncwarp();
+        uint8_t* tile_s = stg + sb * 2048;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int phys = k ^ ((lane >> 1) & 3);  // 64-byte swizzle of the tensor map
+          *reinterpret_cast<uint4*>(tile_s + lane * 64 + phys * 16) =
+              make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+        }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, smem_addr(tile_s), col0, row0);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        sb ^= 1;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
   } else {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------ epilogue (LSU stores)
+    // Any row pitch (the lm_head output has an odd one): lane == row to stage
+    // the accumulators in shared memory, then lane == column for coalesced
+    // stores of each row segment.
     const int ew = warp - 2;             // 0..7
     const int quad = warp & 3;           // TMEM lane quadrant this warp may access
     const int half = ew >> 2;            // which half of the BN columns
@@ -340,26 +446,28 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with row pitch
 // `ld` elements; box = box_rows x 64 columns, 128-byte swizzle, OOB -> 0.
 static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t ld,
-                    int box_rows) {
+                    int box_rows, int box_cols = BK,
+                    CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto enc = get_encode();
   if (!enc) return fail(GPT_ERR_CUDA, "cuTensorMapEncodeTiled unavailable from the driver");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
-                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(GPT_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
   return GPT_OK;
 }
 
-template <int BN, int EPI>
-static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Params& p, int grid,
-                     cudaStream_t st) {
+template <int BN, int EPI, bool kTmaStore>
+static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm, const Params& p,
+                     int grid, cudaStream_t st) {
   using S = Smem<BN>;
   static_assert(S::kTotal <= 232448, "shared memory budget exceeded");
-  auto kern = gemm_tc_kernel<BN, EPI>;
+  static_assert(S::kEpiBytes >= kEpiWarps * 4096, "TMA-store staging does not fit");
+  auto kern = gemm_tc_kernel<BN, EPI, kTmaStore>;
   // Attribute set per device the first time this instantiation runs there.
   static bool done[64] = {false};
   static std::mutex mu;
@@ -373,17 +481,17 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Params&
       done[dev] = true;
     }
   }
-  kern<<<grid, kThreads, S::kTotal, st>>>(ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(kThreads), S::kTotal, st, ta, tb, tcm, p);
   return launch_status("gemm_tc");
 }
 
-// Picks BN in {128, 256} minimising (waves x BN), i.e. the busiest SM's
-// MMA work under persistent scheduling.
+// Tile width: 256 unless N is at most 128. Measured on B200 at M = 16384
+// (K = 768 / 3072): BN = 256 is faster for every GPT-2 GEMM, even where the
+// 128-wide tile quantises better over 148 SMs (c_fc + GELU: 77 us vs 118 us).
 static int pick_bn(int64_t M, int64_t N, int sms) {
-  int64_t nm = (M + BM - 1) / BM;
-  int64_t t256 = nm * ((N + 255) / 256), t128 = nm * ((N + 127) / 128);
-  int64_t c256 = ((t256 + sms - 1) / sms) * 256, c128 = ((t128 + sms - 1) / sms) * 128;
-  return (N <= 128 || c128 < c256) ? 128 : 256;
+  (void)M;
+  (void)sms;
+  return N <= 128 ? 128 : 256;
 }
 
 int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const void* R, int64_t ldr,
@@ -391,6 +499,12 @@ int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const
   int sms = device_sm_count();
   if (sms <= 0) return fail(GPT_ERR_CUDA, "no CUDA device");
   int bn = pick_bn(M, N, sms);
+  // GPT_GEMM_BN=128|256 overrides the tile width (tuning experiments).
+  static const int forced_bn = [] {
+    const char* e = getenv("GPT_GEMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced_bn == 128 || forced_bn == 256) bn = forced_bn;
   CUtensorMap ta, tb;
   int s = make_map(&ta, A, M, K, lda, BM);
   if (s) return s;
@@ -410,17 +524,28 @@ int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const
   p.ldr = ldr;
   p.ldc = ldc;
   int grid = p.num_tiles < sms ? p.num_tiles : sms;
-#define GPT_TC_EPI(BNV)                                                         \
-  switch (epi) {                                                                \
-    case GPT_EPI_NONE: return launch_bn<BNV, GPT_EPI_NONE>(ta, tb, p, grid, st); \
-    case GPT_EPI_BIAS: return launch_bn<BNV, GPT_EPI_BIAS>(ta, tb, p, grid, st); \
-    case GPT_EPI_BIAS_GELU: return launch_bn<BNV, GPT_EPI_BIAS_GELU>(ta, tb, p, grid, st); \
-    default: return launch_bn<BNV, GPT_EPI_BIAS_RESIDUAL>(ta, tb, p, grid, st); \
+  // TMA-store epilogue when C (and R) rows are 16-byte aligned; otherwise LSU stores.
+  const bool tma_store = aligned(C, 16) && (ldc * 2) % 16 == 0 &&
+                         (epi != GPT_EPI_BIAS_RESIDUAL || (aligned(R, 16) && (ldr * 2) % 16 == 0)) &&
+                         (epi == GPT_EPI_NONE || aligned(bias, 16));
+  CUtensorMap tcm;
+  if (tma_store) {
+    s = make_map(&tcm, C, M, N, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (s) return s;
+  } else {
+    tcm = ta;  // unused by the LSU-store epilogue
+  }
+#define GPT_TC_EPI(BNV, TS)                                                                         \
+  switch (epi) {                                                                                    \
+    case GPT_EPI_NONE: return launch_bn<BNV, GPT_EPI_NONE, TS>(ta, tb, tcm, p, grid, st);           \
+    case GPT_EPI_BIAS: return launch_bn<BNV, GPT_EPI_BIAS, TS>(ta, tb, tcm, p, grid, st);           \
+    case GPT_EPI_BIAS_GELU: return launch_bn<BNV, GPT_EPI_BIAS_GELU, TS>(ta, tb, tcm, p, grid, st); \
+    default: return launch_bn<BNV, GPT_EPI_BIAS_RESIDUAL, TS>(ta, tb, tcm, p, grid, st);            \
   }
   if (bn == 256) {
-    GPT_TC_EPI(256)
+    if (tma_store) { GPT_TC_EPI(256, true) } else { GPT_TC_EPI(256, false) }
   } else {
-    GPT_TC_EPI(128)
+    if (tma_store) { GPT_TC_EPI(128, true) } else { GPT_TC_EPI(128, false) }
   }
 #undef GPT_TC_EPI
 }

@@ -2,6 +2,7 @@
 #include "capi.cu"
 #include "elementwise.cu"
 #include "gemm_tc.cu"
+#include "gemm_skinny.cu"
 #include "gemm_simt.cu"
 #include "attention.cu"
 #include "decode.cu"

@@ -276,3 +276,20 @@ def test_argmax_and_advance(dtype):
     ops.decode_advance(tok, pos, seq)
     assert pos.item() == 4
     assert torch.equal(seq[:, 4].cpu(), ref)
+
+
+# ----------------------------------------------------------------- few-row (decode) GEMM: cluster split-K
+@pytest.mark.parametrize("epi", EPIS)
+@pytest.mark.parametrize("M,N,K", [(64, 2304, 768), (64, 768, 3072), (8, 768, 768), (1, 50257, 768),
+                                   (200, 3072, 768), (256, 1000, 1600), (17, 130, 48), (64, 768, 768)])
+def test_gemm_few_rows(epi, M, N, K):
+    dtype = torch.bfloat16
+    a = randn(M, K, seed=50).to(dtype).cuda()
+    w = (randn(N, K, seed=51) / math.sqrt(K)).to(dtype).cuda()
+    bias = randn(N, seed=52).to(dtype).cuda()
+    for it in range(2):
+        r = randn(M, N, seed=53 + it).to(dtype).cuda()
+        ref = gemm_ref(a.cpu(), w.cpu(), bias.cpu(), r.cpu(), epi)
+        out = r.clone() if epi == L.EPI_BIAS_RESIDUAL else torch.empty((M, N), dtype=dtype, device="cuda")
+        ops.gemm(a, w, out, bias=bias, resid=out if epi == L.EPI_BIAS_RESIDUAL else None, epilogue=epi)
+        assert rel_err(out, ref) < BF16_REL, (it, rel_err(out, ref))
