@@ -10,6 +10,8 @@
 // Both read q/k/v through (b, h, t) strides so they consume the fused QKV
 // GEMM output [B, T, 3C] directly and write [B, T, C] for c_proj, removing
 // the split / transpose / contiguous copies of cutile_gpt/models/gpt.py:133-146.
+#include <stdlib.h>
+
 #include "common.cuh"
 
 namespace gpt {
@@ -341,6 +343,13 @@ extern "C" int gpt_attention_prefill(const void* q, const void* k, const void* v
   const float sl2 = scale * kLog2e;
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == GPT_BF16) {
+    // GPT_ATTN_IMPL=mma selects the mma.sync kernel (comparison runs).
+    static const bool force_mma = [] {
+      const char* e = getenv("GPT_ATTN_IMPL");
+      return e && e[0] == 'm';
+    }();
+    if (!force_mma && gpt::attn_tc::eligible(D, q, k, v, out, q_strides, k_strides, v_strides, o_strides))
+      return gpt::attn_tc::launch(q, k, v, out, B, H, T, q_strides, k_strides, v_strides, o_strides, sl2, st);
     auto al = [](const void* p, int64_t s1, int64_t s2, int64_t s3) {
       return gpt::aligned(p, 16) && (s1 % 8) == 0 && (s2 % 8) == 0 && (s3 % 8) == 0;
     };
