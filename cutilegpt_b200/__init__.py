@@ -16,12 +16,32 @@ from .kernels import (
     cutile_causal_attention,
     cutile_fused_mlp,
 )
+from .api import (
+    TileOp,
+    TileConfig,
+    TensorSpec,
+    Layout,
+    DType,
+    tile,
+    configure_tiles,
+    DataProfile,
+    DataAnalyzer,
+)
 from .models import CutileGPT, GPTConfig
 
 __all__ = [
     '__version__',
     'CutileGPT',
     'GPTConfig',
+    'TileOp',
+    'TileConfig',
+    'TensorSpec',
+    'Layout',
+    'DType',
+    'tile',
+    'configure_tiles',
+    'DataProfile',
+    'DataAnalyzer',
     'cutile_gelu',
     'cutile_embedding',
     'cutile_linear',

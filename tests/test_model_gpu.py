@@ -148,3 +148,22 @@ def test_sampling_shapes_and_range():
     g = torch.Generator(device="cuda").manual_seed(0)
     seq = m.generate(ids(3, 5, 300, 19).cuda(), 10, temperature=0.8, top_k=20, generator=g)
     assert seq.shape == (3, 15) and seq.min() >= 0 and seq.max() < 300
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_tile_api_mlp_and_attention_match_oracle(dtype):
+    from cutilegpt_b200 import tile
+    g = torch.Generator().manual_seed(30)
+    C, H = 128, 4
+    x = torch.randn(2, 40, C, generator=g).to(dtype)
+    w1, b1 = (torch.randn(4 * C, C, generator=g) * 0.05).to(dtype), (torch.randn(4 * C, generator=g) * 0.1).to(dtype)
+    w2, b2 = (torch.randn(C, 4 * C, generator=g) * 0.05).to(dtype), (torch.randn(C, generator=g) * 0.1).to(dtype)
+    y = tile(x.cuda()).linear(w1.cuda(), b1.cuda()).gelu().linear(w2.cuda(), b2.cuda()).execute()
+    ref = R.linear(R.gelu(R.linear(x.double(), w1.double(), b1.double())), w2.double(), b2.double())
+    tol = 1e-3 if dtype == torch.float32 else 2e-2
+    assert ((y.double().cpu() - ref).abs().max() / ref.abs().max()).item() < tol
+    qkv = torch.randn(2, 40, 3 * C, generator=g).to(dtype)
+    a = tile(qkv.cuda()).attention(n_head=H).execute()
+    q, k, v = (t.reshape(2, 40, H, C // H).transpose(1, 2) for t in qkv.double().split(C, dim=2))
+    ref = R.causal_attention(q, k, v).transpose(1, 2).reshape(2, 40, C)
+    assert ((a.double().cpu() - ref).abs().max() / ref.abs().max()).item() < tol
