@@ -168,8 +168,9 @@ def run_decode(args, model, cfg, rank, world, dev):
     barrier(world)
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = model._decode_state(hi - lo, P + S)          # the state the timed generate uses
     p0.record()
-    model.generate(prompt, 1, top_k=1)                 # prefill + first token
+    model.forward_last(prompt, out=st.logits, cache=st.cache)   # the prefill inside generate
     p1.record()
     d0.record()
     model.generate(prompt, S, top_k=1)                 # prefill + S-1 graph-replayed decode steps

@@ -50,6 +50,11 @@ SIGNATURES = {
                                     _f32, _p, _i32, _p]),
     "gpt_attention_decode_noalloc": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p,
                                             _f32, _i32, _p]),
+    "gpt_decode_fused_plan_bytes": (_i64, [_i64]),
+    "gpt_decode_fused_workspace_bytes": (_i64, [_i64, _i64]),
+    "gpt_decode_fused_plan": (_i32, [_p, _i64, _p, _i64, _i64]),
+    "gpt_decode_fused": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64,
+                                _p]),
     "gpt_decode_advance": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p]),
     "gpt_argmax": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
 }

@@ -25,6 +25,7 @@ the forward path):
 from __future__ import annotations
 
 import math
+import os
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -52,7 +53,7 @@ class _Workspace:
 class _DecodeState:
     """Buffers of the KV-cache generation loop for one (B, Tmax)."""
 
-    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device):
+    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device, fused: bool = True):
         C, H = cfg.n_embd, cfg.n_head
         D = C // H
         self.B, self.Tmax = B, Tmax
@@ -69,6 +70,11 @@ class _DecodeState:
         nbytes = ops.decode_workspace_bytes(B, H, D, Tmax)
         self.dec_ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=device)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        # fused decode step (one persistent kernel for all blocks), when the shapes allow it
+        self.fused = (fused and dtype == torch.bfloat16 and D == 64 and C % 128 == 0 and C <= 2048 and 1 <= B <= 64)
+        if self.fused:
+            self.fused_ws = torch.zeros((ops.decode_fused_workspace_bytes(B, C),), dtype=torch.uint8, device=device)
+            self.fused_plan = None   # built from the model's weights on first use
 
 
 class CutileGPT:
@@ -87,6 +93,9 @@ class CutileGPT:
         self._dec: Dict[Tuple[int, int], _DecodeState] = {}
         # Optional object with start(flops) / stop() around every GEMM launch.
         self.kernel_timer = None
+        # Single-kernel fused decode step (opt-in, GPT_DECODE_FUSED=1): correct and tested, but on
+        # B200 at B=64 it is still slower than the per-op step (0.90 vs 0.77 ms per GPT-2 124M step).
+        self.fused_decode = os.environ.get("GPT_DECODE_FUSED", "0") == "1"
         self._init_weights(seed)
 
     # ------------------------------------------------------------------ weights
@@ -235,13 +244,20 @@ class CutileGPT:
         if st is None:
             if len(self._dec) >= 2:
                 self._dec.pop(next(iter(self._dec)))
-            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device)
+            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device, fused=self.fused_decode)
             self._dec[key] = st
         return st
 
     def _decode_step(self, st: _DecodeState) -> None:
         """One token per sequence at device position *st.pos: logits into st.logits."""
         cfg = self.config
+        if st.fused:
+            if st.fused_plan is None:
+                st.fused_plan = ops.decode_fused_plan(self.weights, cfg.n_layer, cfg.n_embd, self.device)
+            ops.decode_fused(st.fused_plan, cfg.n_layer, st.tok, st.pos, self._w('wte'), self._w('wpe'),
+                             self._w('ln_f.weight'), self._w('ln_f.bias'), st.cache, st.h, st.fused_ws)
+            self._gemm(st.h, self._w('lm_head.weight'), st.logits)
+            return
         C, H = cfg.n_embd, cfg.n_head
         scale = 1.0 / math.sqrt(C // H)
         B = st.B

@@ -168,6 +168,30 @@ GPT_API int gpt_attention_decode_noalloc(const void* q, int64_t ld_q,
                          int64_t Tmax, int64_t L, const int64_t* len_dev,
                          float scale, int dtype, void* stream);
 
+/* ---- fused decode step (no reference counterpart; see gpt_attention_decode)
+ * All transformer blocks of one decode step for B <= 64 sequences as one
+ * persistent cooperative kernel (bf16, head_dim 64, n_embd % 128 == 0):
+ * embedding of tok[b] at position *pos_dev, then per block LN1 -> QKV ->
+ * K/V append + attention over positions 0..*pos_dev -> c_proj + residual ->
+ * LN2 -> c_fc + GELU -> c_proj + residual, then ln_f into h_out [B, n_embd]
+ * (the lm_head GEMM input). `plan` holds the weight tensor maps and
+ * per-block pointers (gpt_decode_fused_plan, once per set of weights);
+ * `workspace` (gpt_decode_fused_workspace_bytes) must be zero-filled before
+ * its first use and is left zeroed by every call. kv_cache is
+ * [L, 2, B, H, Tmax, 64]. Calls sharing a workspace must not overlap. */
+GPT_API int64_t gpt_decode_fused_plan_bytes(int64_t L);
+GPT_API int64_t gpt_decode_fused_workspace_bytes(int64_t B, int64_t C);
+/* ptrs: 12 device pointers per block, in the order ln1_w, ln1_b, w_qkv,
+ * b_qkv, w_proj, b_proj, ln2_w, ln2_b, w_fc, b_fc, w_proj2, b_proj2. */
+GPT_API int gpt_decode_fused_plan(void* plan, int64_t plan_bytes,
+                          const void* const* ptrs, int64_t L, int64_t C);
+GPT_API int gpt_decode_fused(const void* plan, int64_t L, int64_t C, int64_t B,
+                     int64_t Tmax, const int64_t* tok, const int64_t* pos_dev,
+                     const void* wte, int64_t vocab, const void* wpe,
+                     int64_t n_pos, const void* lnf_w, const void* lnf_b,
+                     void* kv_cache, void* h_out, void* workspace,
+                     int64_t workspace_bytes, void* stream);
+
 /* End of a decode step: seq[b, *pos_dev + 1] = tok[b] for b < B (seq row
  * stride ld_seq, skipped when seq is NULL), then *pos_dev += 1. Positions
  * at or past seq_len are not written. One tiny kernel. */
