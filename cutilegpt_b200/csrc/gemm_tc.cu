@@ -39,6 +39,7 @@ constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 struct Params {
   int M, N, K;
   int num_m, num_n, num_tiles, num_kb;
+  int n_fast;  // tile order: 1 = the N tiles of one row block run together
   const __nv_bfloat16* bias;
   const __nv_bfloat16* resid;
   __nv_bfloat16* C;
@@ -162,11 +163,20 @@ __device__ __forceinline__ constexpr uint32_t idesc_bf16() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N_ >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-template <int BN>
+// Pair mode (kPair): a 2-CTA cluster computes one 256 x BN tile with
+// tcgen05.mma.cta_group::2 (M = 256). Each CTA loads its own 128 A rows and
+// half of the BN W rows, so a CTA streams 128 x 64 + BN/2 x 64 operand
+// elements per k-block instead of 128 x 64 + BN x 64: a third less L2 ->
+// shared-memory traffic per FLOP. The even CTA (leader) issues the MMAs;
+// each CTA's TMEM holds the accumulators of its own 128 rows, which its own
+// epilogue warps drain. All loads are plain per-CTA TMA loads (no multicast);
+// only the MMA completion (tcgen05.commit) is multicast to both CTAs.
+template <int BN, bool kPair>
 struct Smem {
-  static constexpr int kStages = BN >= 256 ? 4 : 6;
+  static constexpr int kBRows = kPair ? BN / 2 : BN;
+  static constexpr int kStages = kPair ? 6 : (BN >= 256 ? 4 : 6);
   static constexpr int kABytes = BM * BK * 2;
-  static constexpr int kBBytes = BN * BK * 2;
+  static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kRingBytes = kStages * kStageBytes;
   static constexpr int kEpiBytes = kEpiWarps * 32 * kStageRowPitch * 4;
@@ -175,12 +185,59 @@ struct Smem {
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
 };
 
-template <int BN, int EPI, bool kTmaStore>
+__device__ __forceinline__ uint32_t cta_rank_in_cluster() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// shared::cluster address of the same shared-memory location in CTA `rank`.
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(local), "r"(rank));
+  return out;
+}
+// Pair-mode TMA load: the bytes land in this CTA's shared memory and are
+// counted on `bar`, which may be the leader CTA's barrier (cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tc_mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accum) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n}\n" ::"r"(
+          d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accum), "r"(z));
+}
+// Arrive on the barrier at this shared-memory offset in both CTAs of the
+// pair once every previously issued MMA of this thread has completed.
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          bar),
+      "h"((uint16_t)0x3)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+template <int BN, int EPI, bool kTmaStore, bool kPair>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
-  using S = Smem<BN>;
+  using S = Smem<BN, kPair>;
   constexpr int kStages = S::kStages;
+  constexpr int kTileM = kPair ? 2 * BM : BM;
   extern __shared__ uint8_t smem_dyn[];
   // 1024-byte alignment is required by the 128B swizzle atoms.
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
@@ -196,6 +253,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  const uint32_t rank = kPair ? cta_rank_in_cluster() : 0u;  // 0 = leader
+  const int first_tile = kPair ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int tile_step = kPair ? (int)(gridDim.x >> 1) : (int)gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -204,7 +264,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_addr(&tfull[a]), 1);
-      mbar_init(smem_addr(&tempty[a]), kEpiWarps);
+      // Pair mode: the leader's accumulator is free once the epilogue warps
+      // of both CTAs have drained it.
+      mbar_init(smem_addr(&tempty[a]), kPair ? 2 * kEpiWarps : kEpiWarps);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -214,17 +276,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
   }
   if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                     smem_addr(tmem_slot)),
-                 "r"((uint32_t)S::kTmemCols));
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    if constexpr (kPair) {
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_addr(tmem_slot)),
+                   "r"((uint32_t)S::kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+    } else {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_addr(tmem_slot)),
+                   "r"((uint32_t)S::kTmemCols));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (kPair) cluster_barrier();  // peer barriers initialised before any remote arrive / TMA
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  // Everything above touched only this CTA's resources; from here on the
-  // kernel reads activations and writes outputs of the stream.
+  // Everything above touched only this CTA's (pair's) resources; from here on
+  // the kernel reads activations and writes outputs of the stream.
   pdl_wait();
   pdl_trigger();
 
@@ -234,29 +304,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile % p.num_m;
-        const int n_blk = tile / p.num_m;
+      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
+        const int m_blk = p.n_fast ? tile / p.num_n : tile % p.num_m;
+        const int n_blk = p.n_fast ? tile % p.num_n : tile / p.num_m;
+        const int a_row = m_blk * kTileM + (int)rank * BM;
+        const int b_row = n_blk * BN + (int)rank * S::kBRows;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) { ok = false; break; }
-          const uint32_t fb = smem_addr(&full[stage]);
-          mbar_expect_tx(fb, S::kStageBytes);
-          tma_load_2d(smem_addr(ringA + stage * S::kABytes), &tmA, fb, kb * BK, m_blk * BM);
-          tma_load_2d(smem_addr(ringB + stage * S::kBBytes), &tmB, fb, kb * BK, n_blk * BN);
+          if constexpr (kPair) {
+            // Both CTAs' bytes are counted on the leader's barrier.
+            const uint32_t fb = cluster_addr(smem_addr(&full[stage]), 0);
+            if (rank == 0) mbar_expect_tx(smem_addr(&full[stage]), 2 * S::kStageBytes);
+            tma_load_2d_pair(smem_addr(ringA + stage * S::kABytes), &tmA, fb, kb * BK, a_row);
+            tma_load_2d_pair(smem_addr(ringB + stage * S::kBBytes), &tmB, fb, kb * BK, b_row);
+          } else {
+            const uint32_t fb = smem_addr(&full[stage]);
+            mbar_expect_tx(fb, S::kStageBytes);
+            tma_load_2d(smem_addr(ringA + stage * S::kABytes), &tmA, fb, kb * BK, a_row);
+            tma_load_2d(smem_addr(ringB + stage * S::kBBytes), &tmB, fb, kb * BK, b_row);
+          }
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16<BN>();
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                 ((uint32_t)(kTileM >> 4) << 24);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < p.num_tiles && ok; tile += gridDim.x) {
+      for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
         if (!mbar_wait(smem_addr(&tempty[acc]), acc_phase ^ 1)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
@@ -268,162 +349,227 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // +32 bytes per K=16 step inside the swizzle atom (encoded >>4).
-            tc_mma(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+            if constexpr (kPair)
+              tc_mma_pair(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0);
+            else
+              tc_mma(d_tmem, ad + (uint64_t)(2 * k), bd + (uint64_t)(2 * k), idesc, (kb | k) != 0);
           }
-          tc_commit(smem_addr(&empty[stage]));  // slot free once these MMAs retire
+          // slot free (in both CTAs) once these MMAs retire
+          if constexpr (kPair) tc_commit_pair(smem_addr(&empty[stage]));
+          else tc_commit(smem_addr(&empty[stage]));
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        tc_commit(smem_addr(&tfull[acc]));  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue(s)
+        if constexpr (kPair) tc_commit_pair(smem_addr(&tfull[acc]));
+        else tc_commit(smem_addr(&tfull[acc]));
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
     }
-  } else if constexpr (kTmaStore) {
-    // ------------------------------------------------------------ epilogue (TMA store)
-    // lane == row: 32 accumulator columns from TMEM, bias / GELU / residual in
-    // registers, packed bf16 into a 32x32 staging tile (64B-swizzled rows),
-    // written by one TMA bulk store per chunk. Two staging tiles per warp so
-    // the next chunk's math overlaps the previous store.
-    const int ew = warp - 2;
-    const int quad = warp & 3;
-    const int half = ew >> 2;
-    uint8_t* stg = reinterpret_cast<uint8_t*>(epi) + ew * 4096;
-    constexpr int kChunksPerHalf = BN / 64;
-    int sb = 0;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      const int m_blk = tile % p.num_m;
-      const int n_blk = tile / p.num_m;
-      if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
-      tc_fence_after();
-      const int row0 = m_blk * BM + quad * 32;
-      const int row = row0 + lane;
-      const bool row_ok = row < p.M;
-      for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
-        const int col0 = n_blk * BN + c * 32;
-        const bool full = col0 + 32 <= p.N;
-        float badd[32], radd[32];
-        if (EPI != GPT_EPI_NONE) {
-          if (full) {
-            load32_bf16(p.bias + col0, badd);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) badd[j] = col0 + j < p.N ? __bfloat162float(p.bias[col0 + j]) : 0.f;
-          }
-        }
+  } else {
+    const uint32_t tempty_leader[2] = {kPair ? cluster_addr(smem_addr(&tempty[0]), 0) : smem_addr(&tempty[0]),
+                                       kPair ? cluster_addr(smem_addr(&tempty[1]), 0) : smem_addr(&tempty[1])};
+    if constexpr (kTmaStore) {
+      // ---------------------------------------------------------- epilogue (TMA store)
+      // lane == row: 32 accumulator columns from TMEM, bias / GELU / residual in
+      // registers, packed bf16 into a 32x32 staging tile (64B-swizzled rows),
+      // written by one TMA bulk store per chunk. Two staging tiles per warp so
+      // the next chunk's math overlaps the previous store.
+      const int ew = warp - 2;
+      const int quad = warp & 3;
+      const int half = ew >> 2;
+      uint8_t* stg = reinterpret_cast<uint8_t*>(epi) + ew * 4096;
+      constexpr int kChunksPerHalf = BN / 64;
+      int sb = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = first_tile; tile < p.num_tiles; tile += tile_step) {
+        const int m_blk = p.n_fast ? tile / p.num_n : tile % p.num_m;
+        const int n_blk = p.n_fast ? tile % p.num_n : tile / p.num_m;
+        const int row0 = m_blk * kTileM + (int)rank * BM + quad * 32;
+        const int row = row0 + lane;
+        const bool row_ok = row < p.M;
+        // The residual row segments of every chunk of this tile are requested
+        // before waiting for the accumulator, so their HBM latency overlaps
+        // the tile's MMAs instead of serialising chunk after chunk.
+        uint4 rraw[kChunksPerHalf][4];
         if (EPI == GPT_EPI_BIAS_RESIDUAL) {
-          const __nv_bfloat16* rp = p.resid + (int64_t)row * p.ldr + col0;
-          if (row_ok && full) {
-            load32_bf16(rp, radd);
-          } else {
 #pragma unroll
-            for (int j = 0; j < 32; ++j) radd[j] = (row_ok && col0 + j < p.N) ? __bfloat162float(rp[j]) : 0.f;
+          for (int cc = 0; cc < kChunksPerHalf; ++cc) {
+            const int col0 = n_blk * BN + (half * kChunksPerHalf + cc) * 32;
+            if (row_ok && col0 + 32 <= p.N) {
+              const uint4* rp = reinterpret_cast<const uint4*>(p.resid + (int64_t)row * p.ldr + col0);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) rraw[cc][i] = __ldg(rp + i);
+            }
           }
         }
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
-        uint32_t pk[16];
+        if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
+        tc_fence_after();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
-          if (EPI != GPT_EPI_NONE) { v0 += badd[2 * j]; v1 += badd[2 * j + 1]; }
-          if (EPI == GPT_EPI_BIAS_GELU) { v0 = gelu_tanh<true>(v0); v1 = gelu_tanh<true>(v1); }
-          if (EPI == GPT_EPI_BIAS_RESIDUAL) { v0 += radd[2 * j]; v1 += radd[2 * j + 1]; }
-          pk[j] = pack2_bf16(v0, v1);
-        }
-        // The store issued from this staging tile two chunks ago must have read it.
-        if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
-        __syncwarp();
-        uint8_t* tile_s = stg + sb * 2048;
+        for (int cc = 0; cc < kChunksPerHalf; ++cc) {
+          const int c = half * kChunksPerHalf + cc;
+          const int col0 = n_blk * BN + c * 32;
+          const bool full = col0 + 32 <= p.N;
+          // bias and residual stay packed (bf16 pairs) until the math loop.
+          uint32_t bw[16], rw[16];
+          if (EPI != GPT_EPI_NONE) {
+            if (full) {
+              const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int phys = k ^ ((lane >> 1) & 3);  // 64-byte swizzle of the tensor map
-          *reinterpret_cast<uint4*>(tile_s + lane * 64 + phys * 16) =
-              make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+              for (int i = 0; i < 4; ++i) {
+                const uint4 v = __ldg(bp + i);
+                bw[4 * i] = v.x; bw[4 * i + 1] = v.y; bw[4 * i + 2] = v.z; bw[4 * i + 3] = v.w;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float lo = col0 + 2 * j < p.N ? __bfloat162float(p.bias[col0 + 2 * j]) : 0.f;
+                const float hi = col0 + 2 * j + 1 < p.N ? __bfloat162float(p.bias[col0 + 2 * j + 1]) : 0.f;
+                bw[j] = pack2_bf16(lo, hi);
+              }
+            }
+          }
+          if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+            if (row_ok && full) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                rw[4 * i] = rraw[cc][i].x; rw[4 * i + 1] = rraw[cc][i].y;
+                rw[4 * i + 2] = rraw[cc][i].z; rw[4 * i + 3] = rraw[cc][i].w;
+              }
+            } else {
+              const __nv_bfloat16* rp = p.resid + (int64_t)row * p.ldr + col0;
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                const float lo = (row_ok && col0 + 2 * j < p.N) ? __bfloat162float(rp[2 * j]) : 0.f;
+                const float hi = (row_ok && col0 + 2 * j + 1 < p.N) ? __bfloat162float(rp[2 * j + 1]) : 0.f;
+                rw[j] = pack2_bf16(lo, hi);
+              }
+            }
+          }
+          uint32_t r[32];
+          tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32), r);
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
+            if (EPI != GPT_EPI_NONE) {
+              const float2 bf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[j]));
+              v0 += bf.x; v1 += bf.y;
+            }
+            if (EPI == GPT_EPI_BIAS_GELU) { v0 = gelu_tanh<true>(v0); v1 = gelu_tanh<true>(v1); }
+            if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+              const float2 rf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw[j]));
+              v0 += rf.x; v1 += rf.y;
+            }
+            pk[j] = pack2_bf16(v0, v1);
+          }
+          // The store issued from this staging tile two chunks ago must have read it.
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+          __syncwarp();
+          uint8_t* tile_s = stg + sb * 2048;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int phys = k ^ ((lane >> 1) & 3);  // 64-byte swizzle of the tensor map
+            *reinterpret_cast<uint4*>(tile_s + lane * 64 + phys * 16) =
+                make_uint4(pk[4 * k], pk[4 * k + 1], pk[4 * k + 2], pk[4 * k + 3]);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, smem_addr(tile_s), col0, row0);
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+          sb ^= 1;
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(&tmC, smem_addr(tile_s), col0, row0);
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          if constexpr (kPair) mbar_arrive_cluster(tempty_leader[acc]);
+          else mbar_arrive(tempty_leader[acc]);
         }
-        sb ^= 1;
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
-    }
-    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
-  } else {
-    // ------------------------------------------------------------ epilogue (LSU stores)
-    // Any row pitch (the lm_head output has an odd one): lane == row to stage
-    // the accumulators in shared memory, then lane == column for coalesced
-    // stores of each row segment.
-    const int ew = warp - 2;             // 0..7
-    const int quad = warp & 3;           // TMEM lane quadrant this warp may access
-    const int half = ew >> 2;            // which half of the BN columns
-    float* stg = epi + ew * 32 * kStageRowPitch;
-    constexpr int kChunks = BN / 32;
-    constexpr int kChunksPerHalf = kChunks / 2;
-    int acc = 0;
-    uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < p.num_tiles; tile += gridDim.x) {
-      const int m_blk = tile % p.num_m;
-      const int n_blk = tile / p.num_m;
-      if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
-      tc_fence_after();
-      const int row0 = m_blk * BM + quad * 32;
-      for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
-        // lane == column in the store phase below.
-        const int col = n_blk * BN + c * 32 + lane;
-        const bool col_ok = col < p.N;
-        // Residual loads for all 32 rows are issued first so their latency
-        // overlaps the TMEM load and the shared-memory transpose.
-        float res[32];
-        if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    } else {
+      // ---------------------------------------------------------- epilogue (LSU stores)
+      // Any row pitch (the lm_head output has an odd one): lane == row to stage
+      // the accumulators in shared memory, then lane == column for coalesced
+      // stores of each row segment.
+      const int ew = warp - 2;             // 0..7
+      const int quad = warp & 3;           // TMEM lane quadrant this warp may access
+      const int half = ew >> 2;            // which half of the BN columns
+      float* stg = epi + ew * 32 * kStageRowPitch;
+      constexpr int kChunks = BN / 32;
+      constexpr int kChunksPerHalf = kChunks / 2;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = first_tile; tile < p.num_tiles; tile += tile_step) {
+        const int m_blk = p.n_fast ? tile / p.num_n : tile % p.num_m;
+        const int n_blk = p.n_fast ? tile % p.num_n : tile / p.num_m;
+        if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
+        tc_fence_after();
+        const int row0 = m_blk * kTileM + (int)rank * BM + quad * 32;
+        for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
+          // lane == column in the store phase below.
+          const int col = n_blk * BN + c * 32 + lane;
+          const bool col_ok = col < p.N;
+          // Residual loads for all 32 rows are issued first so their latency
+          // overlaps the TMEM load and the shared-memory transpose.
+          float res[32];
+          if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+#pragma unroll
+            for (int rr = 0; rr < 32; ++rr) {
+              const int row = row0 + rr;
+              res[rr] = (row < p.M && col_ok) ? __bfloat162float(p.resid[(int64_t)row * p.ldr + col]) : 0.f;
+            }
+          }
+          float bcol = 0.f;
+          if (EPI != GPT_EPI_NONE && col_ok) bcol = __bfloat162float(p.bias[col]);
+          uint32_t r[32];
+          const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32);
+          tmem_ld32(taddr, r);
+          // lane == row: stage the raw accumulators.
+#pragma unroll
+          for (int j = 0; j < 32; ++j) stg[lane * kStageRowPitch + j] = __uint_as_float(r[j]);
+          __syncwarp();
+          // lane == column: bias / GELU / residual, coalesced row stores.
 #pragma unroll
           for (int rr = 0; rr < 32; ++rr) {
             const int row = row0 + rr;
-            res[rr] = (row < p.M && col_ok) ? __bfloat162float(p.resid[(int64_t)row * p.ldr + col]) : 0.f;
+            if (row < p.M && col_ok) {
+              float v = stg[rr * kStageRowPitch + lane] + bcol;
+              if (EPI == GPT_EPI_BIAS_GELU) v = gelu_tanh<true>(v);
+              if (EPI == GPT_EPI_BIAS_RESIDUAL) v += res[rr];
+              p.C[(int64_t)row * p.ldc + col] = __float2bfloat16_rn(v);
+            }
           }
+          __syncwarp();
         }
-        float bcol = 0.f;
-        if (EPI != GPT_EPI_NONE && col_ok) bcol = __bfloat162float(p.bias[col]);
-        uint32_t r[32];
-        const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32);
-        tmem_ld32(taddr, r);
-        // lane == row: stage the raw accumulators.
-#pragma unroll
-        for (int j = 0; j < 32; ++j) stg[lane * kStageRowPitch + j] = __uint_as_float(r[j]);
+        tc_fence_before();
         __syncwarp();
-        // lane == column: bias / GELU / residual, coalesced row stores.
-#pragma unroll
-        for (int rr = 0; rr < 32; ++rr) {
-          const int row = row0 + rr;
-          if (row < p.M && col_ok) {
-            float v = stg[rr * kStageRowPitch + lane] + bcol;
-            if (EPI == GPT_EPI_BIAS_GELU) v = gelu_tanh<true>(v);
-            if (EPI == GPT_EPI_BIAS_RESIDUAL) v += res[rr];
-            p.C[(int64_t)row * p.ldc + col] = __float2bfloat16_rn(v);
-          }
+        if (lane == 0) {
+          if constexpr (kPair) mbar_arrive_cluster(tempty_leader[acc]);
+          else mbar_arrive(tempty_leader[acc]);
         }
-        __syncwarp();
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&tempty[acc]));
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
     }
   }
 
   tc_fence_before();
   __syncthreads();
+  // Pair mode: neither CTA frees its TMEM or shared memory while the peer may
+  // still issue MMAs into it or arrive on its barriers.
+  if constexpr (kPair) cluster_barrier();
   if (warp == 1) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
-                 "r"((uint32_t)S::kTmemCols));
+    if constexpr (kPair)
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"((uint32_t)S::kTmemCols));
+    else
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base),
+                   "r"((uint32_t)S::kTmemCols));
   }
 }
 
@@ -461,13 +607,13 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t col
   return GPT_OK;
 }
 
-template <int BN, int EPI, bool kTmaStore>
+template <int BN, int EPI, bool kTmaStore, bool kPair>
 static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm, const Params& p,
                      int grid, cudaStream_t st) {
-  using S = Smem<BN>;
+  using S = Smem<BN, kPair>;
   static_assert(S::kTotal <= 232448, "shared memory budget exceeded");
   static_assert(S::kEpiBytes >= kEpiWarps * 4096, "TMA-store staging does not fit");
-  auto kern = gemm_tc_kernel<BN, EPI, kTmaStore>;
+  auto kern = gemm_tc_kernel<BN, EPI, kTmaStore, kPair>;
   // Attribute set per device the first time this instantiation runs there.
   static bool done[64] = {false};
   static std::mutex mu;
@@ -481,7 +627,10 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
       done[dev] = true;
     }
   }
-  launch_pdl(kern, dim3(grid), dim3(kThreads), S::kTotal, st, ta, tb, tcm, p);
+  if constexpr (kPair)
+    launch_pdl_cluster(kern, dim3(grid), dim3(kThreads), S::kTotal, st, 2u, ta, tb, tcm, p);
+  else
+    launch_pdl(kern, dim3(grid), dim3(kThreads), S::kTotal, st, ta, tb, tcm, p);
   return launch_status("gemm_tc");
 }
 
@@ -492,6 +641,55 @@ static int pick_bn(int64_t M, int64_t N, int sms) {
   (void)M;
   (void)sms;
   return N <= 128 ? 128 : 256;
+}
+
+// Co-resident 2-CTA clusters of the pair kernel on this device (the GPC
+// layout can leave SMs without a partner); the persistent grid never exceeds it.
+static int pair_slots(int sms) {
+  static int cached[64] = {0};
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return sms / 2;
+  std::lock_guard<std::mutex> g(mu);
+  if (cached[dev] == 0) {
+    using S = Smem<256, true>;
+    auto kern = gemm_tc_kernel<256, GPT_EPI_NONE, true, true>;
+    int n = sms / 2;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal) == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * n);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = S::kTotal;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) == cudaSuccess && clusters > 0 && clusters < n)
+        n = clusters;
+    }
+    cudaGetLastError();
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+template <int BN, bool kPair>
+static int launch_epi(int epi, bool tma_store, const CUtensorMap& ta, const CUtensorMap& tb,
+                      const CUtensorMap& tcm, const Params& p, int grid, cudaStream_t st) {
+#define GPT_TC_EPI(TS)                                                                                     \
+  switch (epi) {                                                                                           \
+    case GPT_EPI_NONE: return launch_bn<BN, GPT_EPI_NONE, TS, kPair>(ta, tb, tcm, p, grid, st);           \
+    case GPT_EPI_BIAS: return launch_bn<BN, GPT_EPI_BIAS, TS, kPair>(ta, tb, tcm, p, grid, st);           \
+    case GPT_EPI_BIAS_GELU: return launch_bn<BN, GPT_EPI_BIAS_GELU, TS, kPair>(ta, tb, tcm, p, grid, st); \
+    default: return launch_bn<BN, GPT_EPI_BIAS_RESIDUAL, TS, kPair>(ta, tb, tcm, p, grid, st);            \
+  }
+  if (tma_store) { GPT_TC_EPI(true) } else { GPT_TC_EPI(false) }
+#undef GPT_TC_EPI
 }
 
 int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const void* R, int64_t ldr,
@@ -505,25 +703,41 @@ int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const
     return e ? atoi(e) : 0;
   }();
   if (forced_bn == 128 || forced_bn == 256) bn = forced_bn;
+  // CTA pairs (256-row tiles, cta_group::2) for BN = 256 once there are
+  // enough rows to fill them; GPT_GEMM_PAIR=0 forces single-CTA tiles.
+  static const int pair_env = [] {
+    const char* e = getenv("GPT_GEMM_PAIR");
+    return e ? atoi(e) : -1;
+  }();
+  const bool pair = bn == 256 && sms >= 2 && (pair_env < 0 ? M > BM : pair_env != 0);
+  const int tile_m = pair ? 2 * BM : BM;
   CUtensorMap ta, tb;
   int s = make_map(&ta, A, M, K, lda, BM);
   if (s) return s;
-  s = make_map(&tb, W, N, K, K, bn);
+  s = make_map(&tb, W, N, K, K, pair ? bn / 2 : bn);
   if (s) return s;
   Params p;
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
-  p.num_m = (int)((M + BM - 1) / BM);
+  p.num_m = (int)((M + tile_m - 1) / tile_m);
   p.num_n = (int)((N + bn - 1) / bn);
   p.num_tiles = p.num_m * p.num_n;
   p.num_kb = (int)((K + BK - 1) / BK);
+  // Row blocks of A are read from HBM once either way; the order decides
+  // which operand is re-read from L2. N-fastest keeps one row block of A hot
+  // while every N tile consumes it, which needs all of W resident in L2:
+  // chosen while W is small (every GPT-2 layer weight), otherwise M-fastest
+  // (the 77 MB lm_head weight is then streamed once, A re-read from L2).
+  p.n_fast = (N * K * 2 <= (32ll << 20)) ? 1 : 0;
   p.bias = (const __nv_bfloat16*)bias;
   p.resid = (const __nv_bfloat16*)R;
   p.C = (__nv_bfloat16*)C;
   p.ldr = ldr;
   p.ldc = ldc;
-  int grid = p.num_tiles < sms ? p.num_tiles : sms;
+  const int slots = pair ? pair_slots(sms) : sms;  // persistent CTAs (pairs)
+  int grid = p.num_tiles < slots ? p.num_tiles : slots;
+  if (pair) grid *= 2;
   // TMA-store epilogue when C (and R) rows are 16-byte aligned; otherwise LSU stores.
   const bool tma_store = aligned(C, 16) && (ldc * 2) % 16 == 0 &&
                          (epi != GPT_EPI_BIAS_RESIDUAL || (aligned(R, 16) && (ldr * 2) % 16 == 0)) &&
@@ -535,19 +749,11 @@ int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const
   } else {
     tcm = ta;  // unused by the LSU-store epilogue
   }
-#define GPT_TC_EPI(BNV, TS)                                                                         \
-  switch (epi) {                                                                                    \
-    case GPT_EPI_NONE: return launch_bn<BNV, GPT_EPI_NONE, TS>(ta, tb, tcm, p, grid, st);           \
-    case GPT_EPI_BIAS: return launch_bn<BNV, GPT_EPI_BIAS, TS>(ta, tb, tcm, p, grid, st);           \
-    case GPT_EPI_BIAS_GELU: return launch_bn<BNV, GPT_EPI_BIAS_GELU, TS>(ta, tb, tcm, p, grid, st); \
-    default: return launch_bn<BNV, GPT_EPI_BIAS_RESIDUAL, TS>(ta, tb, tcm, p, grid, st);            \
-  }
   if (bn == 256) {
-    if (tma_store) { GPT_TC_EPI(256, true) } else { GPT_TC_EPI(256, false) }
-  } else {
-    if (tma_store) { GPT_TC_EPI(128, true) } else { GPT_TC_EPI(128, false) }
+    if (pair) return launch_epi<256, true>(epi, tma_store, ta, tb, tcm, p, grid, st);
+    return launch_epi<256, false>(epi, tma_store, ta, tb, tcm, p, grid, st);
   }
-#undef GPT_TC_EPI
+  return launch_epi<128, false>(epi, tma_store, ta, tb, tcm, p, grid, st);
 }
 
 // Whether the tensor-core path can serve this request (TMA: 16-byte

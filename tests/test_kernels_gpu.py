@@ -141,7 +141,8 @@ def gemm_ref(a, w, bias, r, epi):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 @pytest.mark.parametrize("epi", EPIS)
 @pytest.mark.parametrize("M,N,K", [(64, 192, 48), (128, 256, 64), (200, 2304, 768), (300, 768, 3072),
-                                   (129, 50257, 48), (64, 3072, 768), (8, 768, 768), (1000, 129, 1600)])
+                                   (129, 50257, 48), (64, 3072, 768), (8, 768, 768), (1000, 129, 1600),
+                                   (513, 2304, 768), (1000, 50257, 64), (2048, 768, 3072)])
 def test_gemm(dtype, epi, M, N, K):
     a = randn(M, K, seed=10).to(dtype)
     w = (randn(N, K, seed=11) / math.sqrt(K)).to(dtype)
