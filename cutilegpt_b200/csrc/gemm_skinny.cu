@@ -27,6 +27,8 @@ constexpr int kSkMaxSplits = 16;
 struct SkParams {
   int M, N, K, Mp;
   int nkb, kb_per, splits;
+  int stages;  // ring depth: at most kSkStages and the k-blocks per CTA
+  int rows_per;  // split-K: output rows reduced (and stored) by each cluster CTA, a power of two >= 4
   const __nv_bfloat16* bias;
   const __nv_bfloat16* resid;
   __nv_bfloat16* C;
@@ -46,55 +48,93 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+__device__ __forceinline__ void cluster_arrive() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
 }
-// Generic address of the same shared-memory location in cluster CTA `rank`;
-// plain loads through it let the compiler keep many in flight.
-__device__ __forceinline__ const float* peer_ptr(const float* local, uint32_t rank) {
-  uint64_t out;
-  asm("mapa.u64 %0, %1, %2;" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(local)), "r"(rank));
-  return reinterpret_cast<const float*>(out);
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
+__device__ __forceinline__ uint32_t sk_cluster_addr(uint32_t local, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(local), "r"(rank));
+  return out;
+}
+// Shared memory: [ring: stages x (W slab 16 KB + A rows), reused after the
+// main loop as this CTA's fp32 partial [Mp][128]] [split-K receive buffer:
+// splits x rows_per x 128 fp32] [barriers]. The ring holds only as many
+// stages as a CTA has k-blocks: small footprints let the CTAs of the next
+// kernels in the stream become resident early and stream their weight
+// slices while this kernel runs.
+__host__ __device__ inline int sk_ring_bytes(int Mp, int stages, int splits) {
+  const int ring = stages * (128 * BK * 2 + Mp * BK * 2);
+  const int part = splits > 1 ? Mp * 128 * 4 : 0;
+  return ring > part ? ring : part;
+}
+__host__ __device__ inline int sk_recv_bytes(int splits, int rows_per) {
+  return splits > 1 ? splits * 128 * rows_per * 4 : 0;
+}
+__host__ __device__ inline int sk_smem_bytes(int Mp, int stages, int splits, int rows_per) {
+  return 1024 + sk_ring_bytes(Mp, stages, splits) + sk_recv_bytes(splits, rows_per) + (2 * kSkStages + 2) * 8 + 16;
+}
+constexpr int kSkSmemLimit = 232448;
 
-__host__ __device__ inline int sk_ring_bytes(int Mp) { return kSkStages * (128 * BK * 2 + Mp * BK * 2); }
-__host__ __device__ inline int sk_smem_bytes(int Mp) { return 1024 + sk_ring_bytes(Mp) + (2 * kSkStages + 1) * 8 + 16; }
+#ifdef GPT_SK_TRACE
+__device__ unsigned long long g_sk_trace[1024 * 8];
+#define SK_STAMP(i)                                                                  \
+  do {                                                                               \
+    const unsigned cta = blockIdx.x + blockIdx.y * gridDim.x;                        \
+    if (threadIdx.x == 0 && cta < 1024) g_sk_trace[cta * 8 + (i)] = global_timer_ns(); \
+  } while (0)
+#else
+#define SK_STAMP(i) \
+  do {              \
+  } while (0)
+#endif
 
 template <int EPI>
-__global__ void __launch_bounds__(kSkThreads)
+__global__ void __launch_bounds__(kSkThreads, 4)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                        const SkParams p) {
+  SK_STAMP(0);
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
   constexpr int kWBytes = 128 * BK * 2;
   const int aBytes = p.Mp * BK * 2;
+  const int stages = p.stages;
   uint8_t* ringW = base;
-  uint8_t* ringA = base + kSkStages * kWBytes;
-  // After the main loop the ring is idle and holds this CTA's fp32 partial
-  // [Mp][128] (Mp*512 bytes <= ring size for every Mp).
-  float* part = reinterpret_cast<float*>(base);
-  uint64_t* bars = (uint64_t*)(base + sk_ring_bytes(p.Mp));
+  uint8_t* ringA = base + stages * kWBytes;
+  float* part = reinterpret_cast<float*>(base);  // after the main loop
+  float* recv = reinterpret_cast<float*>(base + sk_ring_bytes(p.Mp, stages, p.splits));
+  uint64_t* bars = (uint64_t*)(base + sk_ring_bytes(p.Mp, stages, p.splits) + sk_recv_bytes(p.splits, p.rows_per));
   uint64_t* full = bars;
   uint64_t* empty = bars + kSkStages;
   uint64_t* done = bars + 2 * kSkStages;
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kSkStages + 1);
+  uint64_t* recv_full = bars + 2 * kSkStages + 1;
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * kSkStages + 2);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x;
-  const int split = p.splits > 1 ? (int)cluster_ctarank() : 0;
+  const bool clustered = p.splits > 1;
+  const int split = clustered ? (int)cluster_ctarank() : 0;
   const int n0 = tile * 128;
   const int kb0 = split * p.kb_per;
   const int kb1 = min(p.nkb, kb0 + p.kb_per);
   const uint32_t tcols = p.Mp <= 32 ? 32u : p.Mp <= 64 ? 64u : p.Mp <= 128 ? 128u : 256u;
+  // Split-K: this CTA reduces rows [r_lo, r_lo + r_cnt) of the padded Mp rows.
+  const int r_lo = split * p.rows_per;
+  const int r_cnt = clustered ? max(0, min(p.rows_per, p.Mp - r_lo)) : 0;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kSkStages; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(smem_addr(&full[s]), 1);
       mbar_init(smem_addr(&empty[s]), 1);
     }
     mbar_init(smem_addr(done), 1);
+    mbar_init(smem_addr(recv_full), 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    // every cluster CTA sends its partial of these rows: splits x 128 x r_cnt fp32
+    if (r_cnt > 0) mbar_expect_tx(smem_addr(recv_full), (uint32_t)(p.splits * 128 * r_cnt * 4));
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
@@ -103,6 +143,12 @@ __global__ void __launch_bounds__(kSkThreads)
   }
   tc_fence_before();
   __syncthreads();
+  // Receive barriers of the whole cluster are initialised before any CTA
+  // sends (this overlaps the previous kernel: it precedes griddepcontrol.wait).
+  if (clustered) {
+    cluster_arrive();
+    cluster_wait();
+  }
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
@@ -113,25 +159,27 @@ __global__ void __launch_bounds__(kSkThreads)
     // Weights do not depend on earlier kernels: the first ring slots are
     // filled with W before waiting for the previous kernel (programmatic
     // dependent launch), the activation rows after.
-    const int pre = min(kb1 - kb0, kSkStages);
+    const int pre = min(kb1 - kb0, stages);
     for (int i = 0; i < pre; ++i) {
       const uint32_t fb = smem_addr(&full[i]);
       mbar_expect_tx(fb, bytes);
       tma_load_2d(smem_addr(ringW + i * kWBytes), &tmW, fb, (kb0 + i) * BK, n0);
     }
+    SK_STAMP(1);
     pdl_wait();
     pdl_trigger();
+    SK_STAMP(2);
     for (int i = 0; i < pre; ++i)
       tma_load_2d(smem_addr(ringA + i * aBytes), &tmA, smem_addr(&full[i]), (kb0 + i) * BK, 0);
-    int stage = pre % kSkStages;
-    uint32_t phase = pre == kSkStages ? 1u : 0u;
+    int stage = pre % stages;
+    uint32_t phase = pre == stages ? 1u : 0u;
     for (int kb = kb0 + pre; kb < kb1; ++kb) {
       if (!mbar_wait(smem_addr(&empty[stage]), phase ^ 1)) break;
       const uint32_t fb = smem_addr(&full[stage]);
       mbar_expect_tx(fb, bytes);
       tma_load_2d(smem_addr(ringW + stage * kWBytes), &tmW, fb, kb * BK, n0);
       tma_load_2d(smem_addr(ringA + stage * aBytes), &tmA, fb, kb * BK, 0);
-      if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+      if (++stage == stages) { stage = 0; phase ^= 1; }
     }
   } else if (warp == 1 && lane == 0) {
     // kind::f16, D fp32, A = W slab (128 rows), B = activation rows (Mp), both K-major.
@@ -148,21 +196,22 @@ __global__ void __launch_bounds__(kSkThreads)
       for (int k = 0; k < BK / 16; ++k)
         tc_mma(tmem, wd + (uint64_t)(2 * k), ad + (uint64_t)(2 * k), idesc, (kb > kb0 || k > 0) ? 1u : 0u);
       tc_commit(smem_addr(&empty[stage]));
-      if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+      if (++stage == stages) { stage = 0; phase ^= 1; }
     }
     tc_commit(smem_addr(done));  // also covers an empty K slice (no MMA issued)
   }
   __syncwarp();
   if (!(warp == 0 && lane == 0)) pdl_wait();
-  const bool ok = mbar_wait(smem_addr(done), 0);
-  tc_fence_after();
 
-  const int nl = warp * 32 + lane;  // row of the W slab == TMEM lane
+  const int nl = warp * 32 + lane;  // row of the W slab == TMEM lane == output column
   const int n = n0 + nl;
   const bool n_ok = n < p.N;
   const bool has_k = kb1 > kb0;
   const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-  if (p.splits == 1) {
+  if (!clustered) {
+    const bool ok = mbar_wait(smem_addr(done), 0);
+    tc_fence_after();
+    SK_STAMP(3);
     for (int c = 0; c < p.Mp && ok; c += 32) {
       uint32_t r[32];
       tmem_ld32(lane_base + (uint32_t)c, r);
@@ -173,7 +222,25 @@ __global__ void __launch_bounds__(kSkThreads)
       }
     }
   } else {
-    // own partial -> shared memory (the ring is no longer read by TMA or MMA)
+    // Bias and residual of this CTA's output rows are fetched while the
+    // partials are still being produced.
+    constexpr int kMaxPre = 8;
+    float bcol = 0.f;
+    if (EPI != GPT_EPI_NONE && n_ok) bcol = __bfloat162float(p.bias[n]);
+    float rpre[kMaxPre];
+    if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+#pragma unroll
+      for (int j = 0; j < kMaxPre; ++j) {
+        const int m = r_lo + j;
+        rpre[j] = (j < r_cnt && m < p.M && n_ok) ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+      }
+    }
+    const bool ok = mbar_wait(smem_addr(done), 0);
+    tc_fence_after();
+    SK_STAMP(3);
+    // Push: the partial goes to shared memory as [Mp][128] (lane == column,
+    // conflict-free), then one bulk copy per owner CTA moves its contiguous
+    // row block into slot [split] of the owner's receive buffer.
     for (int c = 0; c < p.Mp; c += 32) {
       uint32_t r[32];
       if (ok && has_k) tmem_ld32(lane_base + (uint32_t)c, r);
@@ -181,32 +248,84 @@ __global__ void __launch_bounds__(kSkThreads)
       for (int j = 0; j < 32; ++j)
         if (c + j < p.Mp) part[(c + j) * 128 + nl] = (ok && has_k) ? __uint_as_float(r[j]) : 0.f;
     }
-    cluster_sync();  // every partial of the cluster is visible
-    const int mchunk = (p.M + p.splits - 1) / p.splits;
-    const int m_lo = split * mchunk, m_hi = min(p.M, m_lo + mchunk);
-    float bn = 0.f;
-    if (EPI != GPT_EPI_NONE && n_ok) bn = __bfloat162float(p.bias[n]);
-    for (int m0 = m_lo; m0 < m_hi; m0 += 8) {
-      float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int s = 0; s < p.splits; ++s) {
-        const float* src = peer_ptr(part, (uint32_t)s) + m0 * 128 + nl;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (m0 + j < m_hi) v[j] += src[j * 128];
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int d = 0; d * p.rows_per < p.Mp; ++d) {
+        const int rows = min(p.rows_per, p.Mp - d * p.rows_per);
+        const uint32_t src = smem_addr(part + d * p.rows_per * 128);
+        const uint32_t dst = sk_cluster_addr(smem_addr(recv + split * p.rows_per * 128), (uint32_t)d);
+        const uint32_t bar = sk_cluster_addr(smem_addr(recv_full), (uint32_t)d);
+        asm volatile(
+            "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+            "r"(src), "r"((uint32_t)(rows * 128 * 4)), "r"(bar)
+            : "memory");
       }
+    }
+    SK_STAMP(4);
+    bool got = true;
+    if (r_cnt > 0) {
+      got = mbar_wait(smem_addr(recv_full), 0);
+      SK_STAMP(5);
+    }
+    // Every owner has received its rows, so every bulk copy has finished
+    // reading its source: no CTA leaves while a peer still copies from it.
+    cluster_arrive();
+    if (r_cnt > 0) {
+      // thread nl: column n, rows r_lo .. r_lo + r_cnt; fixed summation order.
+      auto finish = [&](int j0, const float4& acc, const float* radd) {
+        const float o4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int m = m0 + j;
-        if (m < m_hi && n_ok) {
-          float x = v[j] + bn;
-          if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
-          if (EPI == GPT_EPI_BIAS_RESIDUAL) x += __bfloat162float(p.resid[(int64_t)m * p.ldr + n]);
-          p.C[(int64_t)m * p.ldc + n] = __float2bfloat16_rn(x);
+        for (int e = 0; e < 4; ++e) {
+          const int m = r_lo + j0 + e;
+          if (m < p.M && n_ok) {
+            float x = o4[e] + bcol;
+            if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
+            if (EPI == GPT_EPI_BIAS_RESIDUAL) x += radd[e];
+            p.C[(int64_t)m * p.ldc + n] = __float2bfloat16_rn(x);
+          }
+        }
+      };
+      auto reduce4 = [&](int j0) {
+        // slot [sidx][j][128]: lane == column, conflict-free. All slots are
+        // read before the first add (no load-use chain across peers).
+        float v[kSkMaxSplits][4];
+#pragma unroll
+        for (int sidx = 0; sidx < kSkMaxSplits; ++sidx) {
+          if (sidx < p.splits) {
+            const float* bs = recv + (sidx * p.rows_per + j0) * 128 + nl;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[sidx][e] = bs[e * 128];
+          }
+        }
+        float4 acc = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
+#pragma unroll
+        for (int sidx = 1; sidx < kSkMaxSplits; ++sidx)
+          if (sidx < p.splits) {
+            acc.x += v[sidx][0]; acc.y += v[sidx][1]; acc.z += v[sidx][2]; acc.w += v[sidx][3];
+          }
+        return acc;
+      };
+      if (got) {
+#pragma unroll
+        for (int j0 = 0; j0 < kMaxPre; j0 += 4)
+          if (j0 < r_cnt) finish(j0, reduce4(j0), &rpre[j0]);
+        for (int j0 = kMaxPre; j0 < r_cnt; j0 += 4) {
+          float radd[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int m = r_lo + j0 + e;
+            radd[e] = (EPI == GPT_EPI_BIAS_RESIDUAL && m < p.M && n_ok)
+                          ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+          }
+          finish(j0, reduce4(j0), radd);
         }
       }
     }
-    cluster_sync();  // peers have finished reading this CTA's shared memory
+    SK_STAMP(6);
+    cluster_wait();
   }
+  SK_STAMP(7);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -216,17 +335,22 @@ __global__ void __launch_bounds__(kSkThreads)
 }
 
 struct SkPlan {
-  int Mp, tiles, nkb, kb_per, splits;
+  int Mp, tiles, nkb, kb_per, splits, stages, rows_per;
 };
 
-// Splits: enough CTAs for about two per SM, at most the cluster size limit,
-// never an empty K slice.
+// Splits: enough CTAs for about two per three SMs, at most the cluster size
+// limit, never an empty K slice. Each cluster CTA then reduces rows_per output rows
+// (a power of two, at least 4, splits x rows_per >= Mp); the ring gets as
+// many stages as fit beside the receive buffer.
 inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits) {
   SkPlan pl;
   pl.Mp = (int)(((M + 15) / 16) * 16);
   pl.tiles = (int)((N + 127) / 128);
   pl.nkb = (int)((K + BK - 1) / BK);
-  int want = (2 * sms + pl.tiles - 1) / pl.tiles;
+  // About two CTAs for every three SMs: measured on B200 (M = 64, GPT-2
+  // shapes, CUDA-graph replay) this beats one or two per SM, since the next
+  // kernel's CTAs need room to become resident while this one runs.
+  int want = (2 * sms / 3 + pl.tiles - 1) / pl.tiles;
   static const int forced = [] {
     const char* e = getenv("GPT_SKINNY_SPLITS");
     return e ? atoi(e) : 0;
@@ -235,8 +359,16 @@ inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits) 
   if (want > max_splits) want = max_splits;
   if (want > pl.nkb) want = pl.nkb;
   if (want < 1) want = 1;
-  pl.kb_per = (pl.nkb + want - 1) / want;
-  pl.splits = (pl.nkb + pl.kb_per - 1) / pl.kb_per;
+  while (true) {
+    pl.kb_per = (pl.nkb + want - 1) / want;
+    pl.splits = (pl.nkb + pl.kb_per - 1) / pl.kb_per;
+    pl.rows_per = 4;
+    while (pl.splits > 1 && pl.rows_per * pl.splits < pl.Mp) pl.rows_per *= 2;
+    pl.stages = pl.kb_per < kSkStages ? pl.kb_per : kSkStages;
+    while (pl.stages > 1 && sk_smem_bytes(pl.Mp, pl.stages, pl.splits, pl.rows_per) > kSkSmemLimit) --pl.stages;
+    if (sk_smem_bytes(pl.Mp, pl.stages, pl.splits, pl.rows_per) <= kSkSmemLimit || want == 1) break;
+    want = want > 2 ? want / 2 : 1;
+  }
   return pl;
 }
 
@@ -275,7 +407,8 @@ static int sk_setup(int* max_splits) {
   std::lock_guard<std::mutex> g(mu);
   if (cached[dev] == 0) {
     auto kern = gemm_skinny_kernel<EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sk_smem_bytes(kSkMaxM));
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           kSkSmemLimit);
     if (e != cudaSuccess) return fail(GPT_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     // Clusters above 8 CTAs are non-portable; they are used only when the
     // attribute is accepted and a 16-CTA cluster of the largest footprint fits.
@@ -284,7 +417,7 @@ static int sk_setup(int* max_splits) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(1, kSkMaxSplits, 1);
       cfg.blockDim = dim3(kSkThreads, 1, 1);
-      cfg.dynamicSmemBytes = (size_t)sk_smem_bytes(kSkMaxM);
+      cfg.dynamicSmemBytes = (size_t)kSkSmemLimit;
       cudaLaunchAttribute attr[1];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 1;
@@ -321,7 +454,9 @@ static int gemm_skinny_epi(const void* A, int64_t lda, const void* W, const SkPa
   p.nkb = pl.nkb;
   p.kb_per = pl.kb_per;
   p.splits = pl.splits;
-  return sk_launch<EPI>(tw, ta, p, pl.tiles, sk_smem_bytes(pl.Mp), st);
+  p.stages = pl.stages;
+  p.rows_per = pl.rows_per;
+  return sk_launch<EPI>(tw, ta, p, pl.tiles, sk_smem_bytes(pl.Mp, p.stages, p.splits, p.rows_per), st);
 }
 
 // Serves bf16 requests with M <= kSkMaxM rows.
@@ -346,3 +481,9 @@ int gemm_skinny(const void* A, int64_t lda, const void* W, const void* bias, con
 
 }  // namespace tc
 }  // namespace gpt
+
+#ifdef GPT_SK_TRACE
+extern "C" GPT_API int gpt_debug_sk_trace(void* host) {
+  return (int)cudaMemcpyFromSymbol(host, gpt::tc::g_sk_trace, sizeof(gpt::tc::g_sk_trace));
+}
+#endif

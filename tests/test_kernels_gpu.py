@@ -279,6 +279,25 @@ def test_argmax_and_advance(dtype):
     assert torch.equal(seq[:, 4].cpu(), ref)
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_argmax_edge_rows(dtype):
+    V = 50257
+    x = randn(6, V, seed=41).to(dtype)
+    x[0, 5] = x[0, 5 + 1024] = x[0, 5 + 8 * 1024 + 3] = 50.0       # ties across threads / unroll slots
+    x[1, :] = float("-inf")                                        # all -inf -> index 0
+    x[2, 0] = float("nan"); x[2, 777] = 60.0; x[2, 900] = float("nan")   # NaN never wins
+    x[3, V - 1] = 70.0                                             # last element
+    x[4, :] = float("nan"); x[4, 12345] = -3.0                     # the only number wins
+    tok = torch.empty(6, dtype=torch.int64, device="cuda")
+    ops.argmax(x.cuda(), tok)
+    assert tok.cpu().tolist()[:5] == [5, 0, 777, V - 1, 12345]
+    assert tok[5].item() == x[5].float().argmax().item()
+    small = randn(64, 3, seed=42).to(dtype)
+    tok64 = torch.empty(64, dtype=torch.int64, device="cuda")
+    ops.argmax(small.cuda(), tok64)
+    assert torch.equal(tok64.cpu(), small.float().argmax(-1))
+
+
 # ----------------------------------------------------------------- few-row (decode) GEMM: cluster split-K
 @pytest.mark.parametrize("epi", EPIS)
 @pytest.mark.parametrize("M,N,K", [(64, 2304, 768), (64, 768, 3072), (8, 768, 768), (1, 50257, 768),
