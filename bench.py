@@ -42,7 +42,13 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 METRIC = "GPT-2 124M prefill tokens/s (B32xT512 per GPU, bf16)"
+METRIC_XL = "GPT-2 XL prefill tokens/s (B64xT1024 global, bf16)"
 UNIT = "tokens/s"
+
+
+def model_cfg(name):
+    from cutilegpt_b200.models.config import GPTConfig
+    return GPTConfig.gpt2_xl() if name == "xl" else GPTConfig.gpt2()
 
 
 def flops_per_token(cfg, T):
@@ -158,9 +164,14 @@ def barrier(world):
 
 # --------------------------------------------------------------------------- ours
 def run_decode(args, model, cfg, rank, world, dev):
-    """batch 64 sharded over the ranks, prompt 128, 128 greedy KV-cache steps."""
+    """batch 64 sharded over the ranks, prompt 128, 128 greedy KV-cache steps.
+
+    With --model xl (config 5): batch 64, prompt 768, 256 greedy KV-cache steps. The config's own
+    1024-token prompt already fills the context, so every step would re-encode a full window (a
+    prefill per step); the shortened prompt is the named deviation that keeps 768 + 256 <= 1024.
+    """
     from cutilegpt_b200.distributed import shard_range
-    Bg, P, S = 64, 128, 128
+    Bg, P, S = (64, 768, 256) if args.model == "xl" else (64, 128, 128)
     lo, hi = shard_range(Bg, rank, world)
     g2 = torch.Generator().manual_seed(77)
     prompt = torch.randint(0, cfg.vocab_size, (Bg, P), generator=g2)[lo:hi].to(dev)
@@ -205,8 +216,13 @@ def run_ours(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
-    cfg = GPTConfig.gpt2()
-    B, T = args.batch, args.seq
+    cfg = model_cfg(args.model)
+    if args.model == "xl":                             # config 5: global batch 64, sharded (strong scaling)
+        lo, hi = shard_range(args.batch, rank, world)
+        B = hi - lo
+    else:                                              # config 3: 32 sequences per GPU (weak scaling)
+        B = args.batch
+    T = args.seq
     model = CutileGPT(cfg, dtype=torch.bfloat16, device=dev, seed=1234)   # same weights on every rank
     if args.decode_only:
         return {"dec": run_decode(args, model, cfg, rank, world, dev)}
@@ -240,7 +256,7 @@ def run_ours(args, rank, world, local):
     ms = e0.elapsed_time(e1)
     clk = clocks.stop()
     ms_max = max_over_ranks(ms, world)
-    tokens = B * T * args.steps * world
+    tokens = (args.batch if args.model == "xl" else B * world) * T * args.steps
     value = tokens / (ms_max / 1e3)
     gemm_ms = timer.total_ms()
     gemm_launches = len(timer.pairs)
@@ -275,21 +291,20 @@ def run_ours(args, rank, world, local):
 
 
 # --------------------------------------------------------------------------- CPU
-def _cpu_oracle(seq):
-    from cutilegpt_b200.models.config import GPTConfig
+def _cpu_oracle(seq, model="gpt2"):
     from cutilegpt_b200.models.init import init_state
     from oracle import ref_gpt as R
-    cfg = GPTConfig.gpt2()
+    cfg = model_cfg(model)
     w = R.cast_weights(init_state(cfg, 1234), dtype=torch.float32, round_to=torch.bfloat16)
     idx = torch.randint(0, cfg.vocab_size, (1, seq), generator=torch.Generator().manual_seed(5))
     return lambda: R.gpt_forward(w, cfg.n_layer, cfg.n_head, idx)
 
 
-def cpu_sample(seq=512, budget_s=20.0):
-    """Tokens/s of the fp32 CPU oracle (bf16-rounded weights) on one 512-token sequence, all host threads."""
+def cpu_sample(seq=512, budget_s=20.0, model="gpt2"):
+    """Tokens/s of the fp32 CPU oracle (bf16-rounded weights) on one sequence, all host threads."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    fwd = _cpu_oracle(seq)
+    fwd = _cpu_oracle(seq, model)
     times = []
     t_start = time.perf_counter()
     with torch.no_grad():
@@ -307,21 +322,24 @@ def run_reference(args, rank):
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    fwd = _cpu_oracle(args.seq)
+    seq = 128 if args.model == "xl" else args.seq
+    fwd = _cpu_oracle(seq, args.model)
     with torch.no_grad():
         fwd()
         t0 = time.perf_counter()
         for _ in range(args.steps):
             fwd()
         dt = time.perf_counter() - t0
-    value = args.seq * args.steps / dt
-    sample = f"one sequence of {args.seq} tokens per step, fp32 oracle with bf16-rounded weights"
-    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+    value = seq * args.steps / dt
+    xl = args.model == "xl"
+    sample = f"one sequence of {seq} tokens per step, fp32 oracle with bf16-rounded weights"
+    line = {"impl": "reference", "metric": METRIC_XL if xl else METRIC, "value": value, "unit": UNIT,
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong" if xl else "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random weights, uniform random token ids)",
-            "config": {"workload": "cfg3 gpt2-124M prefill (CPU sample: 1x512 tokens per step)",
-                       "model": "gpt2-124M", "seq_len": args.seq},
+            "config": {"workload": (f"cfg5 gpt2-xl prefill (CPU sample: 1x{seq} tokens per step)" if xl else
+                                    f"cfg3 gpt2-124M prefill (CPU sample: 1x{seq} tokens per step)"),
+                       "model": "gpt2-xl" if xl else "gpt2-124M", "seq_len": seq},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "note": "the reference (CuPy + cuTile) cannot be installed on this image; the CPU restatement "
@@ -335,13 +353,19 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=32)
-    ap.add_argument("--seq", type=int, default=512)
+    ap.add_argument("--model", choices=["gpt2", "xl"], default="gpt2",
+                    help="gpt2: config 3/4 (default, the headline); xl: config 5 (GPT-2 XL architecture)")
+    ap.add_argument("--batch", type=int, default=None, help="default 32 per GPU (gpt2), 64 global (xl)")
+    ap.add_argument("--seq", type=int, default=None, help="default 512 (gpt2), 1024 (xl)")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--decode-only", action="store_true", help="only the config-4 decode run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.batch is None:
+        args.batch = 64 if args.model == "xl" else 32
+    if args.seq is None:
+        args.seq = 1024 if args.model == "xl" else 512
 
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
@@ -356,24 +380,32 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return
+    def xl_or(a, b):
+        return a if args.model == "xl" else b
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, cores, n = cpu_sample(args.seq)
+        cseq = 128 if args.model == "xl" else args.seq   # XL: a shorter sequence keeps the sample bounded
+        v, cores, n = cpu_sample(cseq, model=args.model)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"GPT-2 124M fp32 CPU oracle (bf16-rounded weights), 1 sequence x {args.seq} tokens, "
-                         f"median of {n} forwards"}
+               "sample": f"{xl_or('GPT-2 XL', 'GPT-2 124M')} fp32 CPU oracle (bf16-rounded weights), "
+                         f"1 sequence x {cseq} tokens, median of {n} forwards"}
     if rank == 0:
         peak_tf, _, src = load_peaks()
         achieved = r["gemm_flops"] / (r["gemm_ms"] / 1e3) / 1e12
         line = {
-            "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True, "scaling": "weak",
+            "metric": xl_or(METRIC_XL, METRIC), "value": r["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True,
+            "scaling": xl_or("strong", "weak"),
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, uniform random token ids)",
-            "config": {"workload": "cfg3 gpt2-124M prefill, logits at all positions",
-                       "model": "gpt2-124M", "global_batch": args.batch * world, "seq_len": args.seq,
+            "config": {"workload": xl_or("cfg5 gpt2-xl prefill, logits at all positions",
+                                         "cfg3 gpt2-124M prefill, logits at all positions"),
+                       "model": xl_or("gpt2-xl", "gpt2-124M"),
+                       "global_batch": xl_or(args.batch, args.batch * world), "seq_len": args.seq,
                        "parallelism": f"dp{world} (batch-sharded replicas)",
-                       "l2": "inputs larger than L2 (weights 249 MB, logits 1.65 GB per step); no flush"},
+                       "l2": xl_or("inputs larger than L2 (weights 3.1 GB, logits 6.6 GB per step); no flush",
+                                   "inputs larger than L2 (weights 249 MB, logits 1.65 GB per step); no flush")},
             "roofline": {"kernel": "gemm_tc_kernel (tcgen05 GEMM, all launches)", "bound": "tensor",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
                          "traffic": None, "peak_source": src,

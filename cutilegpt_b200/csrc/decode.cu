@@ -70,33 +70,55 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict
 #pragma unroll
   for (int i = 0; i < V; ++i) acc[i] = 0.f;
 
-  for (int j0 = c0 + warp * KPW; j0 < c1; j0 += kWarps * KPW) {
-    const int j = j0 + grp;
-    const bool ok = j < c1;
-    float kv[V], vv[V];
-    uint4 kr = make_uint4(0, 0, 0, 0), vr = make_uint4(0, 0, 0, 0);
-    if (ok) {
-      kr = *reinterpret_cast<const uint4*>(kb + (int64_t)j * D);
-      vr = *reinterpret_cast<const uint4*>(vb + (int64_t)j * D);
-    }
-    const T* ke = reinterpret_cast<const T*>(&kr);
-    const T* ve = reinterpret_cast<const T*>(&vr);
-    float dot = 0.f;
+  // kUnroll groups of KPW keys per warp step: every K and V vector of the
+  // step is requested before the first dot product, so each lane keeps
+  // 2 x kUnroll 16-byte loads in flight; the running max is updated once per
+  // step.
+  constexpr int kUnroll = 8;
+  for (int j0 = c0 + warp * KPW * kUnroll; j0 < c1; j0 += kWarps * KPW * kUnroll) {
+    uint4 kr[kUnroll], vr[kUnroll];
 #pragma unroll
-    for (int i = 0; i < V; ++i) {
-      kv[i] = Tr<T>::to_f(ke[i]);
-      vv[i] = Tr<T>::to_f(ve[i]);
-      dot = fmaf(qv[i], kv[i], dot);
+    for (int u = 0; u < kUnroll; ++u) {
+      const int j = j0 + u * KPW + grp;
+      kr[u] = make_uint4(0, 0, 0, 0);
+      vr[u] = make_uint4(0, 0, 0, 0);
+      if (j < c1) {
+        kr[u] = __ldcs(reinterpret_cast<const uint4*>(kb + (int64_t)j * D));
+        vr[u] = __ldcs(reinterpret_cast<const uint4*>(vb + (int64_t)j * D));
+      }
+    }
+    float dot[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const T* ke = reinterpret_cast<const T*>(&kr[u]);
+      float d = 0.f;
+#pragma unroll
+      for (int i = 0; i < V; ++i) d = fmaf(qv[i], Tr<T>::to_f(ke[i]), d);
+      dot[u] = d;
     }
 #pragma unroll
-    for (int o = 1; o < LPK; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
-    if (ok) {
-      const float mn = fmaxf(m, dot);
+    for (int u = 0; u < kUnroll; ++u) {
+#pragma unroll
+      for (int o = 1; o < LPK; o <<= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], o);
+      if (j0 + u * KPW + grp >= c1) dot[u] = -INFINITY;  // masked key
+    }
+    float mx = dot[0];
+#pragma unroll
+    for (int u = 1; u < kUnroll; ++u) mx = fmaxf(mx, dot[u]);
+    const float mn = fmaxf(m, mx);
+    if (mn != -INFINITY) {  // at least one live key in this lane's group
       const float a = exp2f(m - mn);
-      const float p = exp2f(dot - mn);
-      l = l * a + p;
+      l *= a;
 #pragma unroll
-      for (int i = 0; i < V; ++i) acc[i] = fmaf(acc[i], a, p * vv[i]);
+      for (int i = 0; i < V; ++i) acc[i] *= a;
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const float pu = exp2f(dot[u] - mn);  // 0 for a masked key
+        l += pu;
+        const T* ve = reinterpret_cast<const T*>(&vr[u]);
+#pragma unroll
+        for (int i = 0; i < V; ++i) acc[i] = fmaf(pu, Tr<T>::to_f(ve[i]), acc[i]);
+      }
       m = mn;
     }
   }

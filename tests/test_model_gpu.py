@@ -83,6 +83,25 @@ def test_gpt2_cfg3_bf16_logits():
     assert err.item() < 2e-2, err.item()
 
 
+def test_xl_dims_cfg5_bf16_logits_and_greedy():
+    """BASELINE config 5 widths (GPT-2 XL: C=1600, H=25, D=64, MLP 6400), 2 of its 48 layers so the
+    fp64 oracle finishes in seconds; bf16 logits and the KV-cache greedy path against the oracle."""
+    xl = GPTConfig.gpt2_xl()
+    cfg = GPTConfig(n_layer=2, n_head=xl.n_head, n_embd=xl.n_embd, vocab_size=xl.vocab_size,
+                    block_size=xl.block_size)
+    m, w = make(cfg, torch.bfloat16, seed=12, affine=13)
+    idx = ids(2, 300, cfg.vocab_size, 14)
+    logits, _ = m(idx.cuda())
+    wb = R.cast_weights(w, round_to=torch.bfloat16)
+    ref = R.gpt_forward(wb, cfg.n_layer, cfg.n_head, idx)
+    err = (logits.double().cpu() - ref).abs().max() / ref.abs().max()
+    assert err.item() < 2e-2, err.item()
+    seq = m.generate(idx[:, :40].cuda(), 16, top_k=1).cpu()
+    noise = 2e-2 * ref.abs().max().item()
+    bad, gap = teacher_forced_check(wb, cfg, seq, 40, noise)
+    assert not bad.any(), f"non-tie divergence; gaps {gap[bad]} noise {noise}"
+
+
 def test_greedy_32_fp32_matches_oracle():
     cfg = GPTConfig(n_layer=4, n_head=4, n_embd=128, vocab_size=50257, block_size=256)
     m, w = make(cfg, torch.float32, seed=6, affine=7)
