@@ -57,6 +57,7 @@ SIGNATURES = {
                                 _p]),
     "gpt_decode_advance": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p]),
     "gpt_argmax": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
+    "gpt_sample": (_i32, [_p, _i64, _i64, _i64, ctypes.c_float, _i64, _p, _p, _i64, _p, _i32, _p]),
 }
 
 _lib = None

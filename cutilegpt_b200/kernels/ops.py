@@ -132,6 +132,21 @@ def argmax(logits: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     return out
 
 
+def sample(logits: torch.Tensor, out: torch.Tensor, temperature: float = 1.0, top_k: int | None = None,
+           seed_dev: torch.Tensor | None = None, step_dev: torch.Tensor | None = None, step0: int = 0) -> torch.Tensor:
+    """logits [B, V] -> out int64 [B]: temperature, top-k and a multinomial draw in one kernel.
+
+    The draw of row b is fixed by (seed_dev[0], b, step0 + step_dev[0]); both tensors are int64 on the
+    device (or None = 0), so the call can be captured in a CUDA graph.
+    """
+    B, V = logits.shape
+    k = 0 if top_k is None else int(top_k)
+    L.check(L.lib().gpt_sample(_ptr(logits), _row_stride(logits, "sample"), B, V, float(temperature), k,
+                               _ptr(seed_dev), _ptr(step_dev), int(step0), _ptr(out),
+                               L.dtype_code(logits.dtype), L.stream_ptr()), "gpt_sample")
+    return out
+
+
 def decode_advance(tok: torch.Tensor, pos_dev: torch.Tensor, seq: torch.Tensor | None = None) -> None:
     """seq[b, *pos_dev + 1] = tok[b]; *pos_dev += 1 (one tiny kernel)."""
     B = tok.numel()

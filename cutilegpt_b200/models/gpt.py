@@ -69,7 +69,9 @@ class _DecodeState:
         self.seq = torch.empty((B, Tmax), dtype=torch.int64, device=device)
         nbytes = ops.decode_workspace_bytes(B, H, D, Tmax)
         self.dec_ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=device)
-        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.graph: Optional[torch.cuda.CUDAGraph] = None          # greedy step
+        self.sample_graphs: Dict[Tuple[float, int], torch.cuda.CUDAGraph] = {}   # per (temperature, top_k)
+        self.seed = torch.zeros((1,), dtype=torch.int64, device=device)   # RNG seed of the sampling kernel
         # fused decode step (one persistent kernel for all blocks), when the shapes allow it
         self.fused = (fused and dtype == torch.bfloat16 and D == 64 and C % 128 == 0 and C <= 2048 and 1 <= B <= 64)
         if self.fused:
@@ -285,16 +287,24 @@ class CutileGPT:
         ops.argmax(st.logits, st.tok)
         ops.decode_advance(st.tok, st.pos, seq)
 
+    def _sample_step(self, st: _DecodeState, seq: torch.Tensor, temperature: float, top_k: Optional[int]) -> None:
+        """Decode step + the sampling kernel; the draw is keyed by (seed, row, position of the token)."""
+        self._decode_step(st)
+        ops.sample(st.logits, st.tok, temperature, top_k, st.seed, st.pos)
+        ops.decode_advance(st.tok, st.pos, seq)
+
+    @staticmethod
+    def _new_seed(generator: Optional[torch.Generator]) -> torch.Tensor:
+        """A 62-bit seed drawn from `generator` (or torch's default RNG), so torch.manual_seed reproduces runs."""
+        dev = generator.device if generator is not None else torch.device('cpu')
+        return torch.randint(0, 2 ** 62, (1,), generator=generator, device=dev, dtype=torch.int64)
+
     def _sample(self, logits: torch.Tensor, temperature: float, top_k: Optional[int],
                 generator: Optional[torch.Generator]) -> torch.Tensor:
-        """Temperature / top-k / multinomial draw (gpt.py:207-225), batched over rows."""
-        logits = logits.float() / temperature
-        if top_k is not None:
-            k = min(top_k, logits.shape[-1])
-            kth = torch.topk(logits, k, dim=-1).values[:, -1:]
-            logits = logits.masked_fill(logits < kth, float('-inf'))
-        probs = torch.softmax(logits, dim=-1)
-        return torch.multinomial(probs, 1, generator=generator).squeeze(1)
+        """Temperature / top-k / multinomial draw (gpt.py:207-225) for every row, one kernel launch."""
+        out = torch.empty((logits.shape[0],), dtype=torch.int64, device=logits.device)
+        seed = self._new_seed(generator).to(logits.device)
+        return ops.sample(logits, out, temperature, top_k, seed)
 
     @torch.no_grad()
     def generate(self, idx, max_new_tokens: int, temperature: float = 1.0, top_k: Optional[int] = None,
@@ -322,15 +332,28 @@ class CutileGPT:
         if greedy:
             ops.argmax(st.logits, st.tok)
         else:
-            st.tok.copy_(self._sample(st.logits, temperature, top_k, generator))
+            if temperature <= 0:
+                raise ValueError("temperature must be > 0")
+            st.seed.copy_(self._new_seed(generator))
+            # the draw for the token after position T0 - 1; decode steps use the device position
+            ops.sample(st.logits, st.tok, temperature, top_k, st.seed, None, step0=T0 - 1)
         seq[:, T0] = st.tok
         st.pos.fill_(T0)
         steps = max_new_tokens - 1
         if not greedy:
-            for _ in range(steps):
-                self._decode_step(st)
-                st.tok.copy_(self._sample(st.logits, temperature, top_k, generator))
-                ops.decode_advance(st.tok, st.pos, seq)
+            key = (float(temperature), 0 if top_k is None else int(top_k))
+            g = st.sample_graphs.get(key)
+            if not use_cuda_graph or (g is None and steps < 2):
+                for _ in range(steps):
+                    self._sample_step(st, seq, temperature, top_k)
+            else:
+                if g is None:
+                    self._sample_step(st, seq, temperature, top_k)
+                    steps -= 1
+                    g = self._capture_fn(lambda: self._sample_step(st, st.seq, temperature, top_k))
+                    st.sample_graphs[key] = g
+                for _ in range(steps):
+                    g.replay()
         elif not use_cuda_graph or steps < 2:
             for _ in range(steps):
                 self._greedy_step(st, seq)
@@ -344,15 +367,18 @@ class CutileGPT:
                 st.graph.replay()
         return seq.clone()
 
-    def _capture(self, st: _DecodeState) -> None:
+    def _capture_fn(self, fn) -> torch.cuda.CUDAGraph:
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(device=self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self._greedy_step(st, st.seq)
+                fn()
         torch.cuda.current_stream(self.device).wait_stream(s)
-        st.graph = g
+        return g
+
+    def _capture(self, st: _DecodeState) -> None:
+        st.graph = self._capture_fn(lambda: self._greedy_step(st, st.seq))
 
     def _generate_reforward(self, idx, max_new_tokens, temperature, top_k, generator) -> torch.Tensor:
         """Reference semantics without a cache: re-run the (cropped) prefix each step."""

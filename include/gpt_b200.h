@@ -204,6 +204,20 @@ GPT_API int gpt_decode_advance(const int64_t* tok, int64_t B, int64_t* seq,
 GPT_API int gpt_argmax(const void* logits, int64_t ld, int64_t B, int64_t V,
                int64_t* out, int dtype, void* stream);
 
+/* Sampling step of generate() with temperature / top_k
+ * (cutile_gpt/models/gpt.py:207-225: logits / temperature, top-k mask of
+ * values below the k-th largest, softmax, multinomial draw), one launch for
+ * all B rows: out[b] = drawn token id. top_k <= 0 or >= V keeps every value;
+ * temperature must be > 0. The uniform of row b is a function of
+ * (*seed_dev, b, step0 + *step_dev) (SplitMix64), so equal inputs draw equal
+ * tokens and a captured CUDA graph draws fresh ones as *step_dev advances;
+ * seed_dev / step_dev may be NULL (read as 0). Parity with the reference is
+ * distributional (its CuPy RNG stream cannot be reproduced). */
+GPT_API int gpt_sample(const void* logits, int64_t ld, int64_t B, int64_t V,
+               float temperature, int64_t top_k, const uint64_t* seed_dev,
+               const int64_t* step_dev, int64_t step0, int64_t* out, int dtype,
+               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -313,3 +313,75 @@ def test_gemm_few_rows(epi, M, N, K):
         out = r.clone() if epi == L.EPI_BIAS_RESIDUAL else torch.empty((M, N), dtype=dtype, device="cuda")
         ops.gemm(a, w, out, bias=bias, resid=out if epi == L.EPI_BIAS_RESIDUAL else None, epilogue=epi)
         assert rel_err(out, ref) < BF16_REL, (it, rel_err(out, ref))
+
+
+# ----------------------------------------------------------------- sampling (temperature / top-k / multinomial)
+def _draw(row, n_rows, steps, temperature=1.0, top_k=None, seed=1234):
+    """n_rows copies of one logits row, `steps` launches -> all drawn ids (CPU int64)."""
+    x = row.view(1, -1).expand(n_rows, -1).contiguous().cuda()
+    out = torch.empty(n_rows, dtype=torch.int64, device="cuda")
+    seed_t = torch.tensor([seed], dtype=torch.int64, device="cuda")
+    got = []
+    for s in range(steps):
+        ops.sample(x, out, temperature, top_k, seed_t, None, step0=s)
+        got.append(out.cpu().clone())
+    return torch.cat(got)
+
+
+def _chi2_ok(counts, probs, n):
+    """Pearson chi-square over the support, compared with a loose bound (k - 1 + 6 sqrt(2(k-1)))."""
+    exp = probs * n
+    k = int((probs > 0).sum())
+    stat = (((counts - exp) ** 2) / exp.clamp_min(1e-12))[probs > 0].sum().item()
+    return stat < (k - 1) + 6 * math.sqrt(2 * (k - 1)), stat
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("temperature,top_k", [(1.0, None), (0.5, None), (1.0, 3), (2.0, 5)])
+def test_sample_distribution(dtype, temperature, top_k):
+    V = 50257
+    ids = torch.tensor([7, 100, 2048, 30000, 50256, 12, 999, 4444])
+    vals = torch.tensor([2.0, 1.5, 1.0, 0.5, 0.0, -0.5, -1.0, -2.0])
+    row = torch.full((V,), -40.0)
+    row[ids] = vals
+    row = row.to(dtype)
+    n = 4096 * 6
+    got = _draw(row, 4096, 6, temperature, top_k)
+    z = row.float()[ids] / temperature
+    if top_k is not None:
+        z[top_k:] = float("-inf")                       # vals are sorted: the top-k are the first k
+    probs = torch.softmax(z.double(), 0)
+    assert torch.isin(got, ids[probs > 0]).all()        # mass outside the set (e^-40) never drawn at this n
+    counts = torch.stack([(got == i).sum() for i in ids]).double()
+    ok, stat = _chi2_ok(counts, probs, n)
+    assert ok, (stat, counts, probs * n)
+
+
+def test_sample_deterministic_in_seed_and_step():
+    row = randn(50257, seed=60).bfloat16()
+    a = _draw(row, 64, 2, 1.0, 40, seed=5)
+    b = _draw(row, 64, 2, 1.0, 40, seed=5)
+    c = _draw(row, 64, 2, 1.0, 40, seed=6)
+    assert torch.equal(a, b)
+    assert not torch.equal(a, c)
+    assert not torch.equal(a[:64], a[64:])             # another step draws afresh
+
+
+def test_sample_edges():
+    V = 1000
+    x = torch.full((4, V), -5.0)
+    x[0, [3, 10, 11]] = torch.tensor([5.0, 3.0, 3.0])  # top_k=2: the tie at the threshold stays in
+    x[1, :] = float("-inf")                             # nothing finite -> 0
+    x[2, :] = float("nan"); x[2, 77] = 1.0              # NaN never drawn
+    x[3, 500] = 50.0                                    # one dominant value
+    out = torch.empty(4, dtype=torch.int64, device="cuda")
+    seen0 = set()
+    seed = torch.tensor([9], dtype=torch.int64, device="cuda")
+    for s in range(200):
+        ops.sample(x.cuda(), out, 1.0, 2, seed, None, step0=s)
+        o = out.cpu().tolist()
+        seen0.add(o[0])
+        assert o[1] == 0 and o[2] == 77 and o[3] == 500
+    assert seen0 == {3, 10, 11}
+    with pytest.raises(Exception):
+        ops.sample(x.cuda(), out, 0.0, None)
