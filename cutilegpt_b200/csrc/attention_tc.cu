@@ -3,10 +3,12 @@
 // (cutile_gpt/kernels/attention.py:24-116).
 //
 // Persistent: one CTA per SM walks 128-row query tiles (heaviest causal
-// spans first). Warp 8 lane 0 is the TMA producer and MMA issuer, running
-// ahead through a 3-stage K/V ring and double-buffered S / P / O; warps 0-7
-// do the softmax, query row r owned by threads r and r + 128 (TMEM lane r,
-// one half of the columns each). Per key block of 128:
+// spans first). Warp 9 lane 0 streams Q / K / V by TMA (3-stage K/V ring,
+// double-buffered Q: the next tile's Q is loaded while the current tile
+// runs); warp 8 lane 0 issues the MMAs into double-buffered S / P / O; warps
+// 0-7 do the softmax, query row r owned by threads r and r + 128 (TMEM lane
+// r, one half of the columns each; GPT_ATTN_SOFTMAX_WARPS=16 splits a row
+// over four threads, measured slower on B200). Per key block of 128:
 //   S = Q Kᵀ        tcgen05.mma M=128 N=128 K=64 into one of two TMEM S
 //                   buffers; S_{j+1} is issued before the softmax of S_j
 //   softmax         one tcgen05.ld pass per thread (64 scores), causal /
@@ -39,12 +41,19 @@ using tc::tmem_ld32;
 constexpr int kRows = 128;   // query rows per CTA
 constexpr int kKeys = 128;   // keys per block
 constexpr int kD = 64;
-constexpr int kSoftmaxWarps = 8;
-constexpr int kThreads = (kSoftmaxWarps + 1) * 32;  // 8 softmax warps + producer/MMA warp
+#ifndef GPT_ATTN_SOFTMAX_WARPS
+#define GPT_ATTN_SOFTMAX_WARPS 8
+#endif
+constexpr int kSoftmaxWarps = GPT_ATTN_SOFTMAX_WARPS;
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;  // softmax warps + MMA warp + TMA warp
+constexpr int kSplit = kSoftmaxWarps / 4;           // threads per query row (TMEM lane)
+constexpr int kSC = 128 / kSplit;                   // score columns per thread
+constexpr int kOC = 64 / kSplit;                    // output columns per thread
 constexpr int kTileBytes = kRows * kD * 2;   // 16 KB (Q, K or V tile)
 constexpr int kPBytes = kRows * kKeys * 2;   // 32 KB (two 64-key swizzled sub-tiles)
 constexpr int kKvStages = 3;
-constexpr int kSmem = 1024 + kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + 256;
+constexpr int kQStages = 2;
+constexpr int kSmem = 1024 + kQStages * kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + 256;
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
                                             int c2, int c3) {
@@ -70,7 +79,33 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void softmax_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+// Diagnostics build only (-DGPT_ATTN_TRACE): %globaltimer at fixed points of
+// CTA 0 (producer lane and softmax thread 0), read back with gpt_debug_attn_trace().
+#ifdef GPT_ATTN_TRACE
+__device__ unsigned long long g_at_trace[2][256][4];
+#define AT_STAMP(who, blk, i)                                                          \
+  do {                                                                                 \
+    if (blockIdx.x == 0 && (blk) < 256) g_at_trace[who][blk][i] = global_timer_ns();   \
+  } while (0)
+#else
+#define AT_STAMP(who, blk, i) \
+  do {                        \
+  } while (0)
+#endif
+
+__device__ __forceinline__ void softmax_bar() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
+}
+
+// 32 lanes x 16 consecutive fp32 TMEM columns.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
 
 // Walks one CTA's work: tiles t = blockIdx.x, +gridDim.x, ... (tile t = query
 // block n_qblk-1 - t/(B*H) of head t%(B*H), heaviest first), and within a
@@ -102,28 +137,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                                                               const Params p) {
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
-  uint8_t* sQ = base;
-  uint8_t* sK = sQ + kTileBytes;                 // [3][16 KB]
-  uint8_t* sV = sK + kKvStages * kTileBytes;     // [3][16 KB]
+  uint8_t* sQ = base;                            // [2][16 KB]: Q of this tile and the next
+  uint8_t* sK = sQ + kQStages * kTileBytes;      // [kKvStages][16 KB]
+  uint8_t* sV = sK + kKvStages * kTileBytes;     // [kKvStages][16 KB]
   uint8_t* sP = sV + kKvStages * kTileBytes;     // [2][32 KB]: keys 0-63 | keys 64-127
   uint64_t* bars = (uint64_t*)(sP + 2 * kPBytes);
-  uint64_t* q_full = bars;                       // 1 (TMA tx)
-  uint64_t* q_empty = bars + 1;                  // 1 (commit after a tile's last S)
-  uint64_t* kv_full = bars + 2;                  // 3 (TMA tx)
-  uint64_t* kv_empty = bars + 5;                 // 3 (commit after PV)
-  uint64_t* s_full = bars + 8;                   // 2 (commit after S)
-  uint64_t* s_free = bars + 10;                  // 2 (8 softmax warps)
-  uint64_t* p_full = bars + 12;                  // 2 (8 softmax warps)
-  uint64_t* o_full = bars + 14;                  // 2 (commit after PV)
-  uint64_t* o_free = bars + 16;                  // 2 (8 softmax warps)
-  uint32_t* tmem_slot = (uint32_t*)(bars + 18);
-  __shared__ float sm_red[2][2][kRows];   // row-max exchange, by block parity
-  __shared__ float sm_l[2][kRows];        // row-sum exchange at the end of a tile
+  uint64_t* q_full = bars;                       // 2 (TMA tx)
+  uint64_t* q_empty = bars + 2;                  // 2 (commit after a tile's last S)
+  uint64_t* kv_full = bars + 4;                  // kKvStages (TMA tx)
+  uint64_t* kv_empty = kv_full + kKvStages;      // kKvStages (commit after PV)
+  uint64_t* s_full = kv_empty + kKvStages;       // 2 (commit after S)
+  uint64_t* s_free = s_full + 2;                 // 2 (softmax warps)
+  uint64_t* p_full = s_free + 2;                 // 2 (softmax warps)
+  uint64_t* o_full = p_full + 2;                 // 2 (commit after PV)
+  uint64_t* o_free = o_full + 2;                 // 2 (softmax warps)
+  uint32_t* tmem_slot = (uint32_t*)(o_free + 2);
+  __shared__ float sm_red[2][kSplit][kRows];   // row-max exchange, by block parity
+  __shared__ float sm_l[kSplit][kRows];        // row-sum exchange at the end of a tile
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    mbar_init(smem_addr(q_full), 1);
-    mbar_init(smem_addr(q_empty), 1);
+    for (int i = 0; i < kQStages; ++i) {
+      mbar_init(smem_addr(&q_full[i]), 1);
+      mbar_init(smem_addr(&q_empty[i]), 1);
+    }
     for (int i = 0; i < kKvStages; ++i) {
       mbar_init(smem_addr(&kv_full[i]), 1);
       mbar_init(smem_addr(&kv_empty[i]), 1);
@@ -151,64 +188,81 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   pdl_trigger();
   bool ok = true;
 
-  if (warp == kSoftmaxWarps) {
-    // ------------------------------------------------ TMA producer + MMA issuer (one lane)
+  if (warp == kSoftmaxWarps + 1) {
+    // ------------------------------------------------ TMA producer (one lane)
+    // Q of a tile (two slots: the next tile's Q arrives while the current tile
+    // runs) and the K/V blocks (kKvStages-deep ring), in the MMA order.
     if (lane == 0) {
-      // kind::f16, D fp32, A/B bf16; S: both K-major, N=128; PV: B MN-major (bit 16), N=64.
-      constexpr uint32_t idS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kKeys >> 3) << 17) |
-                               ((uint32_t)(kRows >> 4) << 24);
-      constexpr uint32_t idO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kD >> 3) << 17) |
-                               ((uint32_t)(kRows >> 4) << 24);
-      Cursor lc, sc, pc;                 // load, S-issue and PV-issue cursors
+      Cursor lc;
       lc.set(blockIdx.x, p);
-      sc.set(blockIdx.x, p);
-      pc.set(blockIdx.x, p);
-      int lg = 0, sg = 0, pg = 0;        // global block counters of the three cursors
-      int qtiles = 0;                    // Q tiles loaded so far
-      auto load_kv = [&]() {             // next K/V block into its ring stage
+      int lg = 0, ql = 0;
+      while (lc.valid && ok) {
+        if (lc.j == 0) {
+          const int slot = ql & 1;
+          if (ql >= kQStages && !mbar_wait(smem_addr(&q_empty[slot]), (uint32_t)(((ql / kQStages) - 1) & 1))) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(smem_addr(&q_full[slot]), kTileBytes);
+          tma_load_4d(smem_addr(sQ + slot * kTileBytes), &tq, smem_addr(&q_full[slot]), 0, lc.h, lc.qb * kRows,
+                      lc.b);
+          ++ql;
+        }
         const int st = lg % kKvStages;
-        if (lg >= kKvStages && ok && !mbar_wait(smem_addr(&kv_empty[st]), (uint32_t)(((lg / kKvStages) - 1) & 1)))
+        if (lg >= kKvStages && !mbar_wait(smem_addr(&kv_empty[st]), (uint32_t)(((lg / kKvStages) - 1) & 1))) {
           ok = false;
+          break;
+        }
         const uint32_t fb = smem_addr(&kv_full[st]);
         mbar_expect_tx(fb, 2 * kTileBytes);
         tma_load_4d(smem_addr(sK + st * kTileBytes), &tk, fb, 0, lc.h, lc.j * kKeys, lc.b);
         tma_load_4d(smem_addr(sV + st * kTileBytes), &tv, fb, 0, lc.h, lc.j * kKeys, lc.b);
         lc.next(p);
         ++lg;
-      };
-      auto load_q = [&](const Cursor& c) {
-        if (qtiles > 0 && ok && !mbar_wait(smem_addr(q_empty), (uint32_t)((qtiles - 1) & 1))) ok = false;
-        mbar_expect_tx(smem_addr(q_full), kTileBytes);
-        tma_load_4d(smem_addr(sQ), &tq, smem_addr(q_full), 0, c.h, c.qb * kRows, c.b);
-        ++qtiles;
-      };
+      }
+    }
+  } else if (warp == kSoftmaxWarps) {
+    // ------------------------------------------------ MMA issuer (one lane)
+    if (lane == 0) {
+      // kind::f16, D fp32, A/B bf16; S: both K-major, N=128; PV: B MN-major (bit 16), N=64.
+      constexpr uint32_t idS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kKeys >> 3) << 17) |
+                               ((uint32_t)(kRows >> 4) << 24);
+      constexpr uint32_t idO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kD >> 3) << 17) |
+                               ((uint32_t)(kRows >> 4) << 24);
+      Cursor sc, pc;                     // S-issue and PV-issue cursors
+      sc.set(blockIdx.x, p);
+      pc.set(blockIdx.x, p);
+      int sg = 0, pg = 0, qs = 0;        // S blocks, PV blocks, tiles whose S started
       auto issue_s = [&]() {
         const int st = sg % kKvStages;
         if (sc.j == 0) {
-          load_q(sc);
-          if (ok && !mbar_wait(smem_addr(q_full), (uint32_t)((qtiles - 1) & 1))) ok = false;
+          if (ok && !mbar_wait(smem_addr(&q_full[qs & 1]), (uint32_t)((qs / kQStages) & 1))) ok = false;
+          ++qs;
         }
+        const int qslot = (qs - 1) & 1;  // this tile's Q slot
         if (ok && !mbar_wait(smem_addr(&kv_full[st]), (uint32_t)((sg / kKvStages) & 1))) ok = false;
         if (ok && !mbar_wait(smem_addr(&s_free[sg & 1]), (uint32_t)(((sg >> 1) & 1) ^ 1))) ok = false;
         if (ok) {
           tc_fence_after();
-          const uint64_t qd = desc_sw128(smem_addr(sQ));
+          const uint64_t qd = desc_sw128(smem_addr(sQ + qslot * kTileBytes));
           const uint64_t kd = desc_sw128(smem_addr(sK + st * kTileBytes));
 #pragma unroll
           for (int k = 0; k < kD / 16; ++k)
             tc_mma(tmem + (uint32_t)((sg & 1) * 128), qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), idS, k > 0);
         }
         tc_commit(smem_addr(&s_full[sg & 1]));
-        if (sc.last_in_tile()) tc_commit(smem_addr(q_empty));   // Q may be replaced once these MMAs retire
+        AT_STAMP(0, sg, 0);
+        if (sc.last_in_tile()) tc_commit(smem_addr(&q_empty[qslot]));   // Q slot free once these MMAs retire
         sc.next(p);
         ++sg;
       };
-      for (int i = 0; i < kKvStages && lc.valid; ++i) load_kv();
       if (sc.valid) issue_s();
       while (pc.valid) {
         if (sc.valid) issue_s();         // the next S overlaps the softmax of block pg
         if (ok && !mbar_wait(smem_addr(&p_full[pg & 1]), (uint32_t)((pg >> 1) & 1))) ok = false;
+        AT_STAMP(0, pg, 1);
         if (ok && !mbar_wait(smem_addr(&o_free[pg & 1]), (uint32_t)(((pg >> 1) & 1) ^ 1))) ok = false;
+        AT_STAMP(0, pg, 2);
         const int st = pg % kKvStages;
         if (ok) {
           tc_fence_after();
@@ -222,33 +276,37 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         }
         tc_commit(smem_addr(&o_full[pg & 1]));
         tc_commit(smem_addr(&kv_empty[st]));
+        AT_STAMP(0, pg, 3);
         pc.next(p);
         ++pg;
-        if (lc.valid) load_kv();         // waits for this stage's PV, then refills it
       }
     }
   } else {
-    // ------------------------------------------------ softmax: threads r and r+128 share query row r
+    // ------------------------------------------------ softmax: threads r, r+128, ... share query row r
+    static_assert((kSC == 32 && kOC == 16) || (kSC == 64 && kOC == 32), "2 or 4 threads per query row");
     const int rl = tid & (kRows - 1);
-    const int half = tid >> 7;
+    const int part = tid >> 7;                       // this thread's quarter of the keys / O columns
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     int g = 0;   // global block counter (same order as the producer)
     for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x) {
       Cursor c;
       c.set(t, p);
       const int row = c.qb * kRows + rl;
-      float o[32];
+      float o[kOC];
 #pragma unroll
-      for (int d = 0; d < 32; ++d) o[d] = 0.f;
+      for (int d = 0; d < kOC; ++d) o[d] = 0.f;
       float m_run = -INFINITY, l_part = 0.f, alpha_prev = 1.f;
       // O_i (relative to m_i) folded into o (relative to m_{i-1}) with alpha_i.
       auto fold_o = [&](int gi, float alpha_i) {
         if (!mbar_wait(smem_addr(&o_full[gi & 1]), (uint32_t)((gi >> 1) & 1))) ok = false;
         tc_fence_after();
-        uint32_t r[32];
-        tmem_ld32(tmem + 256 + (uint32_t)((gi & 1) * 64 + half * 32) + lane_off, r);
+        uint32_t r[kOC];
+        if constexpr (kOC == 16)
+          tmem_ld16(tmem + 256 + (uint32_t)((gi & 1) * 64 + part * kOC) + lane_off, r);
+        else
+          tmem_ld32(tmem + 256 + (uint32_t)((gi & 1) * 64 + part * kOC) + lane_off, r);
 #pragma unroll
-        for (int d = 0; d < 32; ++d) o[d] = o[d] * alpha_i + __uint_as_float(r[d]);
+        for (int d = 0; d < kOC; ++d) o[d] = o[d] * alpha_i + __uint_as_float(r[d]);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(smem_addr(&o_free[gi & 1]));
@@ -256,43 +314,48 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       for (int j = 0; j < c.nblk; ++j, ++g) {
         if (!mbar_wait(smem_addr(&s_full[g & 1]), (uint32_t)((g >> 1) & 1))) ok = false;
         tc_fence_after();
-        const int kbase = j * kKeys + half * 64;
+        if (tid == 0) AT_STAMP(1, g, 0);
+        const int kbase = j * kKeys + part * kSC;
         const bool diag = (j == c.nblk - 1);
-        float sv[64];
-        {
+        float sv[kSC];
+#pragma unroll
+        for (int c2 = 0; c2 < kSC; c2 += 32) {
           uint32_t r[32];
-          tmem_ld32(tmem + (uint32_t)((g & 1) * 128 + half * 64) + lane_off, r);
+          tmem_ld32(tmem + (uint32_t)((g & 1) * 128 + part * kSC + c2) + lane_off, r);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(r[i]);
-          tmem_ld32(tmem + (uint32_t)((g & 1) * 128 + half * 64 + 32) + lane_off, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[32 + i] = __uint_as_float(r[i]);
+          for (int i = 0; i < 32; ++i) sv[c2 + i] = __uint_as_float(r[i]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(smem_addr(&s_free[g & 1]));   // S buffer may be overwritten
         // mask only where needed: the diagonal block and a block past T
         float mx = -INFINITY;
-        if (diag || kbase + 64 > p.T) {
+        if (diag || kbase + kSC > p.T) {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) {
+          for (int i = 0; i < kSC; ++i) {
             const int key = kbase + i;
             if (!(key < p.T && (!diag || key <= row))) sv[i] = -INFINITY;
             mx = fmaxf(mx, sv[i]);
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 64; ++i) mx = fmaxf(mx, sv[i]);
+          for (int i = 0; i < kSC; ++i) mx = fmaxf(mx, sv[i]);
         }
-        sm_red[g & 1][half][rl] = mx * p.scale_log2;   // scale > 0 commutes with max
+        sm_red[g & 1][part][rl] = mx * p.scale_log2;   // scale > 0 commutes with max
+        if (tid == 0) AT_STAMP(1, g, 1);
         softmax_bar();
-        mx = fmaxf(m_run, fmaxf(sm_red[g & 1][0][rl], sm_red[g & 1][1][rl]));
+        if (tid == 0) AT_STAMP(1, g, 2);
+        mx = m_run;
+#pragma unroll
+        for (int s2 = 0; s2 < kSplit; ++s2) mx = fmaxf(mx, sm_red[g & 1][s2][rl]);
         const float mref = mx == -INFINITY ? 0.f : mx;
         const float alpha = ex2(m_run - mref);
         float rs = 0.f;
-        uint8_t* prow = sP + (g & 1) * kPBytes + half * (kRows * 128) + rl * 128;
+        // keys [part*kSC, +kSC): sub-tile (part*kSC)/64 (64 keys, 128B-swizzled
+        // K-major rows), 16-byte chunks from ((part*kSC) % 64) / 8 of row rl
+        uint8_t* prow = sP + (g & 1) * kPBytes + ((part * kSC) >> 6) * (kRows * 128) + rl * 128;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {   // 8 chunks of 8 keys, 128B-swizzled K-major rows
+        for (int q = 0; q < kSC / 8; ++q) {
           uint32_t w[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -302,28 +365,32 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             __nv_bfloat162 bp = __floats2bfloat162_rn(p0, p1);
             w[u] = *reinterpret_cast<uint32_t*>(&bp);
           }
-          *reinterpret_cast<uint4*>(prow + ((q ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          const int chunk = ((part * kSC) & 63) / 8 + q;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         l_part = l_part * alpha + rs;
         m_run = mx;
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(smem_addr(&p_full[g & 1]));
+        if (tid == 0) AT_STAMP(1, g, 3);
         if (j > 0) fold_o(g - 1, alpha_prev);
         alpha_prev = alpha;
       }
       fold_o(g - 1, alpha_prev);
-      // row sum across the two halves (sm_l is written again only after the
-      // next tile's block barriers, which every reader passes first)
-      sm_l[half][rl] = l_part;
+      // row sum across the parts (sm_l is written again only after the next
+      // tile's block barriers, which every reader passes first)
+      sm_l[part][rl] = l_part;
       softmax_bar();
-      const float lsum = sm_l[0][rl] + sm_l[1][rl];
+      float lsum = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < kSplit; ++s2) lsum += sm_l[s2][rl];
       if (ok && row < p.T) {
         const float inv = 1.f / lsum;
         __nv_bfloat16* dst =
-            p.out + (int64_t)c.b * p.osb + (int64_t)c.h * p.osh + (int64_t)row * p.ost + half * 32;
+            p.out + (int64_t)c.b * p.osb + (int64_t)c.h * p.osh + (int64_t)row * p.ost + part * kOC;
 #pragma unroll
-        for (int v = 0; v < 4; ++v) {
+        for (int v = 0; v < kOC / 8; ++v) {
           uint32_t w[4];
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -414,3 +481,9 @@ int launch(const void* q, const void* k, const void* v, void* out, int64_t B, in
 
 }  // namespace attn_tc
 }  // namespace gpt
+
+#ifdef GPT_ATTN_TRACE
+extern "C" GPT_API int gpt_debug_attn_trace(void* host) {
+  return (int)cudaMemcpyFromSymbol(host, gpt::attn_tc::g_at_trace, sizeof(gpt::attn_tc::g_at_trace));
+}
+#endif
