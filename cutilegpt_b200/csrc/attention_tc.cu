@@ -53,7 +53,7 @@ constexpr int kTileBytes = kRows * kD * 2;   // 16 KB (Q, K or V tile)
 constexpr int kPBytes = kRows * kKeys * 2;   // 32 KB (two 64-key swizzled sub-tiles)
 constexpr int kKvStages = 3;
 constexpr int kQStages = 2;
-constexpr int kSmem = 1024 + kQStages * kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + 256;
+constexpr int kSmem = 1024 + kQStages * kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + kTileBytes + 256;
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
                                             int c2, int c3) {
@@ -62,6 +62,14 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
+}
+
+// Output tile (staged in shared memory, 128B-swizzled) -> global by TMA.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, uint32_t src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
 }
 
 struct Params {
@@ -82,7 +90,7 @@ __device__ __forceinline__ float ex2(float x) {
 // Diagnostics build only (-DGPT_ATTN_TRACE): %globaltimer at fixed points of
 // CTA 0 (producer lane and softmax thread 0), read back with gpt_debug_attn_trace().
 #ifdef GPT_ATTN_TRACE
-__device__ unsigned long long g_at_trace[2][256][4];
+__device__ unsigned long long g_at_trace[3][256][4];
 #define AT_STAMP(who, blk, i)                                                          \
   do {                                                                                 \
     if (blockIdx.x == 0 && (blk) < 256) g_at_trace[who][blk][i] = global_timer_ns();   \
@@ -134,6 +142,7 @@ struct Cursor {
 __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_constant__ CUtensorMap tq,
                                                               const __grid_constant__ CUtensorMap tk,
                                                               const __grid_constant__ CUtensorMap tv,
+                                                              const __grid_constant__ CUtensorMap to,
                                                               const Params p) {
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
@@ -141,7 +150,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint8_t* sK = sQ + kQStages * kTileBytes;      // [kKvStages][16 KB]
   uint8_t* sV = sK + kKvStages * kTileBytes;     // [kKvStages][16 KB]
   uint8_t* sP = sV + kKvStages * kTileBytes;     // [2][32 KB]: keys 0-63 | keys 64-127
-  uint64_t* bars = (uint64_t*)(sP + 2 * kPBytes);
+  uint8_t* sO = sP + 2 * kPBytes;                // [16 KB]: output tile staged for the TMA store
+  uint64_t* bars = (uint64_t*)(sO + kTileBytes);
   uint64_t* q_full = bars;                       // 2 (TMA tx)
   uint64_t* q_empty = bars + 2;                  // 2 (commit after a tile's last S)
   uint64_t* kv_full = bars + 4;                  // kKvStages (TMA tx)
@@ -377,18 +387,24 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         if (j > 0) fold_o(g - 1, alpha_prev);
         alpha_prev = alpha;
       }
+      if (tid == 0) AT_STAMP(2, t / gridDim.x, 0);
       fold_o(g - 1, alpha_prev);
+      if (tid == 0) AT_STAMP(2, t / gridDim.x, 1);
       // row sum across the parts (sm_l is written again only after the next
       // tile's block barriers, which every reader passes first)
       sm_l[part][rl] = l_part;
+      // the previous tile's TMA store has finished reading sO before it is rewritten
+      if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       softmax_bar();
       float lsum = 0.f;
 #pragma unroll
       for (int s2 = 0; s2 < kSplit; ++s2) lsum += sm_l[s2][rl];
-      if (ok && row < p.T) {
-        const float inv = 1.f / lsum;
-        __nv_bfloat16* dst =
-            p.out + (int64_t)c.b * p.osb + (int64_t)c.h * p.osh + (int64_t)row * p.ost + part * kOC;
+      if (tid == 0) AT_STAMP(2, t / gridDim.x, 2);
+      {
+        // row rl, columns [part*kOC, +kOC) -> 16-byte chunks of the 128-byte
+        // row, XOR-swizzled by (row & 7) as the tensor map expects
+        const float inv = __fdividef(1.f, lsum);
+        uint8_t* srow = sO + rl * 128;
 #pragma unroll
         for (int v = 0; v < kOC / 8; ++v) {
           uint32_t w[4];
@@ -397,11 +413,21 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             __nv_bfloat162 tt = __floats2bfloat162_rn(o[8 * v + 2 * u] * inv, o[8 * v + 2 * u + 1] * inv);
             w[u] = *reinterpret_cast<uint32_t*>(&tt);
           }
-          *reinterpret_cast<uint4*>(dst + 8 * v) = make_uint4(w[0], w[1], w[2], w[3]);
+          const int chunk = (part * kOC) / 8 + v;
+          *reinterpret_cast<uint4*>(srow + ((chunk ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        softmax_bar();
+        if (tid == 0 && ok) {  // rows past T are clipped by the tensor map
+          tma_store_4d(&to, smem_addr(sO), 0, c.h, c.qb * kRows, c.b);
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        }
+        (void)row;
       }
+      if (tid == 0) AT_STAMP(2, t / gridDim.x, 3);
     }
   }
+  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output tiles written
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
@@ -442,10 +468,11 @@ inline bool eligible(int64_t D, const void* q, const void* k, const void* v, con
 int launch(const void* q, const void* k, const void* v, void* out, int64_t B, int64_t H, int64_t T,
            const int64_t* qs, const int64_t* ks, const int64_t* vs, const int64_t* os, float scale_log2,
            cudaStream_t st) {
-  CUtensorMap mq, mk, mv;
+  CUtensorMap mq, mk, mv, mo;
   int s = make_map4(&mq, q, B, H, T, qs[0], qs[1], qs[2]);
   if (!s) s = make_map4(&mk, k, B, H, T, ks[0], ks[1], ks[2]);
   if (!s) s = make_map4(&mv, v, B, H, T, vs[0], vs[1], vs[2]);
+  if (!s) s = make_map4(&mo, out, B, H, T, os[0], os[1], os[2]);
   if (s) return s;
   static bool done[64] = {false};
   static std::mutex mu;
@@ -475,7 +502,7 @@ int launch(const void* q, const void* k, const void* v, void* out, int64_t B, in
   int sms = device_sm_count();
   if (sms <= 0) sms = 148;
   const int grid = (int)(tiles < sms ? tiles : sms);   // persistent: one CTA per SM
-  launch_pdl(attn_tc_kernel, dim3((unsigned)grid), dim3(kThreads), kSmem, st, mq, mk, mv, p);
+  launch_pdl(attn_tc_kernel, dim3((unsigned)grid), dim3(kThreads), kSmem, st, mq, mk, mv, mo, p);
   return launch_status("attention_tc");
 }
 
