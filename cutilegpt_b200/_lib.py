@@ -30,6 +30,18 @@ _STATUS_NAMES = {
 _i64, _p, _i32, _f32 = ctypes.c_int64, ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 _pi64 = ctypes.POINTER(ctypes.c_int64)
 
+
+
+class GemmFusion(ctypes.Structure):
+    """struct gpt_gemm_fusion (include/gpt_b200.h): optional extras of gpt_gemm_fused."""
+    _fields_ = [
+        ("ln_stats", _p), ("ln_parts", _i64), ("ln_eps", _f32), ("ln_u", _p), ("ln_v", _p),
+        ("row_stats", _p),
+        ("k_cache", _p), ("v_cache", _p), ("kv_heads", _i64), ("kv_dim", _i64), ("kv_tmax", _i64),
+        ("kv_pos0", _i64), ("kv_pos_dev", _p),
+    ]
+
+
 # name -> (restype, argtypes); mirrors include/gpt_b200.h
 SIGNATURES = {
     "gpt_version": (_i32, []),
@@ -58,6 +70,10 @@ SIGNATURES = {
     "gpt_decode_advance": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p]),
     "gpt_argmax": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
     "gpt_sample": (_i32, [_p, _i64, _i64, _i64, ctypes.c_float, _i64, _p, _p, _i64, _p, _i32, _p]),
+    "gpt_gemm_fused": (_i32, [_p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32,
+                              ctypes.POINTER(GemmFusion), _i32, _p]),
+    "gpt_row_stats": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
+    "gpt_lnfold_weights": (_i32, [_p, _p, _p, _p, _i64, _i64, _p, _p, _p, _i32, _p]),
 }
 
 _lib = None

@@ -365,6 +365,62 @@ __global__ void decode_advance_kernel(const int64_t* __restrict__ tok, int64_t B
   if (threadIdx.x == 0) *pos = col;
 }
 
+// ============================================================================
+// Row statistics (sum, sum of squares) of x [M, C]: the LayerNorm statistics
+// a folded decode GEMM consumes (one part). One warp per row.
+// ============================================================================
+template <typename T>
+__global__ void __launch_bounds__(256) row_stats_kernel(const T* __restrict__ x, int64_t ld, int64_t M, int64_t C,
+                                                        float* __restrict__ stats) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const T* xr = x + row * ld;
+  float s1 = 0.f, s2 = 0.f;
+  for (int64_t i = lane; i < C; i += 32) {
+    const float v = Tr<T>::to_f(xr[i]);
+    s1 += v;
+    s2 = fmaf(v, v, s2);
+  }
+  s1 = warp_sum(s1);
+  s2 = warp_sum(s2);
+  if (lane == 0) {
+    stats[row * 2] = s1;
+    stats[row * 2 + 1] = s2;
+  }
+}
+
+// LayerNorm fold of a Linear that follows LayerNorm(gamma, beta): one warp
+// per output row n. Wf[n, k] = W[n, k] * gamma[k] (rounded to T);
+// u[n] = sum_k Wf[n, k]; v[n] = sum_k W[n, k] * beta[k] + bias[n].
+template <typename T>
+__global__ void __launch_bounds__(256) lnfold_kernel(const T* __restrict__ W, const T* __restrict__ gamma,
+                                                     const T* __restrict__ beta, const T* __restrict__ bias,
+                                                     int64_t N, int64_t K, T* __restrict__ Wf,
+                                                     float* __restrict__ u, float* __restrict__ v) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t n = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (n >= N) return;
+  float su = 0.f, sv = 0.f;
+  for (int64_t k = lane; k < K; k += 32) {
+    const float w = Tr<T>::to_f(W[n * K + k]);
+    const T wf = Tr<T>::from_f(w * Tr<T>::to_f(gamma[k]));
+    Wf[n * K + k] = wf;
+    su += Tr<T>::to_f(wf);
+    sv = fmaf(w, Tr<T>::to_f(beta[k]), sv);
+  }
+  su = warp_sum(su);
+  sv = warp_sum(sv);
+  if (lane == 0) {
+    u[n] = su;
+    v[n] = sv + (bias ? Tr<T>::to_f(bias[n]) : 0.f);
+  }
+}
+
 }  // namespace gpt
 
 // ============================================================================
@@ -472,6 +528,39 @@ int gpt_decode_advance(const int64_t* tok, int64_t B, int64_t* seq, int64_t ld_s
   GPT_CHECK_ARG(pos_dev && (B == 0 || tok), "gpt_decode_advance: null pointer");
   gpt::launch_pdl(gpt::decode_advance_kernel, dim3(1), dim3(256), 0, (cudaStream_t)stream, tok, B, seq, ld_seq, seq_len, pos_dev);
   return gpt::launch_status("decode_advance");
+}
+
+int gpt_row_stats(const void* x, int64_t ld, int64_t M, int64_t C, float* stats, int dtype, void* stream) {
+  GPT_CHECK_DTYPE(dtype);
+  GPT_CHECK_SHAPE(M >= 0 && C > 0 && ld >= C, "gpt_row_stats: bad sizes");
+  if (M == 0) return GPT_OK;
+  GPT_CHECK_ARG(x && stats, "gpt_row_stats: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const dim3 grid((unsigned)((M + 7) / 8));
+  if (dtype == GPT_F32)
+    gpt::launch_pdl(gpt::row_stats_kernel<float>, grid, dim3(256), 0, st, (const float*)x, ld, M, C, stats);
+  else
+    gpt::launch_pdl(gpt::row_stats_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, (const __nv_bfloat16*)x, ld, M,
+                    C, stats);
+  return gpt::launch_status("row_stats");
+}
+
+int gpt_lnfold_weights(const void* W, const void* gamma, const void* beta, const void* bias, int64_t N, int64_t K,
+                       void* Wf, float* u, float* v, int dtype, void* stream) {
+  GPT_CHECK_DTYPE(dtype);
+  GPT_CHECK_SHAPE(N >= 0 && K > 0, "gpt_lnfold_weights: bad sizes");
+  if (N == 0) return GPT_OK;
+  GPT_CHECK_ARG(W && gamma && beta && Wf && u && v, "gpt_lnfold_weights: null pointer");
+  cudaStream_t st = (cudaStream_t)stream;
+  const dim3 grid((unsigned)((N + 7) / 8));
+  if (dtype == GPT_F32)
+    gpt::launch_pdl(gpt::lnfold_kernel<float>, grid, dim3(256), 0, st, (const float*)W, (const float*)gamma,
+                    (const float*)beta, (const float*)bias, N, K, (float*)Wf, u, v);
+  else
+    gpt::launch_pdl(gpt::lnfold_kernel<__nv_bfloat16>, grid, dim3(256), 0, st, (const __nv_bfloat16*)W,
+                    (const __nv_bfloat16*)gamma, (const __nv_bfloat16*)beta, (const __nv_bfloat16*)bias, N, K,
+                    (__nv_bfloat16*)Wf, u, v);
+  return gpt::launch_status("lnfold_weights");
 }
 
 }  // extern "C"

@@ -148,3 +148,36 @@ extern "C" int gpt_gemm(const void* A, int64_t lda, const void* W, const void* b
   }
   return gpt::simt::gemm<float>(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
 }
+
+extern "C" int gpt_gemm_fused(const void* A, int64_t lda, const void* W, const void* bias, const void* R,
+                              int64_t ldr, void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue,
+                              const gpt_gemm_fusion* fusion, int dtype, void* stream) {
+  if (!fusion) return gpt_gemm(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, dtype, stream);
+  const gpt_gemm_fusion& f = *fusion;
+  GPT_CHECK_ARG(dtype == GPT_BF16, "gpt_gemm_fused: bf16 only");
+  GPT_CHECK_ARG(epilogue >= GPT_EPI_NONE && epilogue <= GPT_EPI_BIAS_RESIDUAL, "gpt_gemm_fused: bad epilogue %d",
+                epilogue);
+  GPT_CHECK_SHAPE(M >= 0 && N >= 0 && K > 0 && M <= gpt::tc::kSkMaxM && N < (1LL << 31) && K < (1LL << 31),
+                  "gpt_gemm_fused: needs 0 <= M <= %d rows, K > 0 (M=%lld N=%lld K=%lld)", gpt::tc::kSkMaxM,
+                  (long long)M, (long long)N, (long long)K);
+  GPT_CHECK_SHAPE(lda >= K && ldc >= N && (epilogue != GPT_EPI_BIAS_RESIDUAL || ldr >= N),
+                  "gpt_gemm_fused: leading dimension smaller than the row");
+  if (M == 0 || N == 0) return GPT_OK;
+  GPT_CHECK_ARG(A && W && C, "gpt_gemm_fused: null operand");
+  GPT_CHECK_ARG(epilogue != GPT_EPI_BIAS_RESIDUAL || R, "gpt_gemm_fused: residual epilogue needs R");
+  if (f.ln_stats) {
+    GPT_CHECK_ARG(f.ln_u && f.ln_v && f.ln_parts >= 1 && f.ln_eps >= 0.f, "gpt_gemm_fused: incomplete LayerNorm fold");
+    GPT_CHECK_ARG(epilogue != GPT_EPI_BIAS_RESIDUAL, "gpt_gemm_fused: LayerNorm fold with a residual epilogue");
+  } else {
+    GPT_CHECK_ARG(epilogue == GPT_EPI_NONE || bias, "gpt_gemm_fused: epilogue needs bias");
+  }
+  if (f.k_cache || f.v_cache) {
+    GPT_CHECK_ARG(f.k_cache && f.v_cache && f.kv_heads > 0 && f.kv_dim > 0 && f.kv_tmax > 0 && f.kv_pos0 >= 0,
+                  "gpt_gemm_fused: incomplete KV append");
+    GPT_CHECK_SHAPE(N == 3 * f.kv_heads * f.kv_dim, "gpt_gemm_fused: KV append needs N = 3 * heads * dim");
+  }
+  GPT_CHECK_ARG(gpt::tc::tc_eligible(A, lda, W, K, M, N),
+                "gpt_gemm_fused: operands must be 16-byte aligned with 16-byte row pitches");
+  return gpt::tc::gemm_skinny_fused(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, f, (cudaStream_t)stream);
+}
+

@@ -33,6 +33,18 @@ struct SkParams {
   const __nv_bfloat16* resid;
   __nv_bfloat16* C;
   int64_t ldr, ldc;
+  // Fused decode extras (gemm_skinny_kernel<EPI, true> only; each may be null):
+  const float* ln_stats;  // [ln_parts][M][2] (sum, sum of squares) of A's rows: LayerNorm folded in
+  const float* ln_u;      // [N] row sums of the gamma-scaled weight
+  const float* ln_v;      // [N] W . beta + bias (replaces bias)
+  int ln_parts;
+  float ln_eps, ln_inv_k;
+  float* stats_out;       // [ceil(N / 128)][M][2] (sum, sum of squares) of C's stored rows
+  __nv_bfloat16* kc;      // KV-cache append of the K and V columns of a fused QKV output:
+  __nv_bfloat16* vc;      //   [B = M][H][Tmax][D], position kv_pos0 + *kv_pos
+  int kv_C, kv_D, kv_H;
+  int64_t kv_tmax, kv_pos0;
+  const int64_t* kv_pos;
 };
 
 template <int EPI>
@@ -76,7 +88,9 @@ __host__ __device__ inline int sk_recv_bytes(int splits, int rows_per) {
 __host__ __device__ inline int sk_smem_bytes(int Mp, int stages, int splits, int rows_per) {
   return 1024 + sk_ring_bytes(Mp, stages, splits) + sk_recv_bytes(splits, rows_per) + (2 * kSkStages + 2) * 8 + 16;
 }
-constexpr int kSkSmemLimit = 232448;
+// Dynamic shared memory budget: the 227 KB per CTA less room for the fused
+// variant's static arrays (row statistics, LayerNorm mean / rstd).
+constexpr int kSkSmemLimit = 232448 - 8192;
 
 #ifdef GPT_SK_TRACE
 __device__ unsigned long long g_sk_trace[1024 * 8];
@@ -91,7 +105,7 @@ __device__ unsigned long long g_sk_trace[1024 * 8];
   } while (0)
 #endif
 
-template <int EPI>
+template <int EPI, bool kFuse>
 __global__ void __launch_bounds__(kSkThreads, 4)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                        const SkParams p) {
@@ -212,27 +226,89 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     const bool ok = mbar_wait(smem_addr(done), 0);
     tc_fence_after();
     SK_STAMP(3);
-    for (int c = 0; c < p.Mp && ok; c += 32) {
-      uint32_t r[32];
-      tmem_ld32(lane_base + (uint32_t)c, r);
+    if constexpr (kFuse) {
+      // LayerNorm folded in (the host allows no other extra without split-K):
+      // row statistics of all Mp rows into shared memory first.
+      __shared__ float ln_ms[kSkMaxM][2];
+      if (p.ln_stats) {
+        for (int m = threadIdx.x; m < p.M; m += kSkThreads) {
+          float s1 = 0.f, s2 = 0.f;
+          for (int q = 0; q < p.ln_parts; ++q) {
+            s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
+            s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
+          }
+          const float mean = s1 * p.ln_inv_k;
+          ln_ms[m][0] = mean;
+          ln_ms[m][1] = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
+        }
+      }
+      __syncthreads();
+      const float un = (p.ln_stats && n_ok) ? p.ln_u[n] : 0.f;
+      const float vn = (p.ln_stats && n_ok) ? p.ln_v[n] : 0.f;
+      for (int c = 0; c < p.Mp && ok; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + (uint32_t)c, r);
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int m = c + j;
-        if (m < p.M && n_ok) sk_store<EPI>(p, m, n, __uint_as_float(r[j]));
+        for (int j = 0; j < 32; ++j) {
+          const int m = c + j;
+          if (m < p.M && n_ok) {
+            float x = __uint_as_float(r[j]);
+            if (p.ln_stats) x = ln_ms[m][1] * (x - ln_ms[m][0] * un) + vn;
+            else if (EPI != GPT_EPI_NONE) x += __bfloat162float(p.bias[n]);
+            if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
+            if (EPI == GPT_EPI_BIAS_RESIDUAL) x += __bfloat162float(p.resid[(int64_t)m * p.ldr + n]);
+            p.C[(int64_t)m * p.ldc + n] = __float2bfloat16_rn(x);
+          }
+        }
+      }
+    } else {
+      for (int c = 0; c < p.Mp && ok; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(lane_base + (uint32_t)c, r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int m = c + j;
+          if (m < p.M && n_ok) sk_store<EPI>(p, m, n, __uint_as_float(r[j]));
+        }
       }
     }
   } else {
     // Bias and residual of this CTA's output rows are fetched while the
     // partials are still being produced.
-    constexpr int kMaxPre = 8;
+    constexpr int kMaxPre = 4;  // residual rows fetched ahead (the first group of four)
     float bcol = 0.f;
-    if (EPI != GPT_EPI_NONE && n_ok) bcol = __bfloat162float(p.bias[n]);
+    // (with the LayerNorm fold the bias is part of ln_v and the pointer may be null)
+    if (EPI != GPT_EPI_NONE && n_ok && !(kFuse && p.ln_stats)) bcol = __bfloat162float(p.bias[n]);
     float rpre[kMaxPre];
     if (EPI == GPT_EPI_BIAS_RESIDUAL) {
 #pragma unroll
       for (int j = 0; j < kMaxPre; ++j) {
         const int m = r_lo + j;
         rpre[j] = (j < r_cnt && m < p.M && n_ok) ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+      }
+    }
+    // LayerNorm fold: mean / rstd of this CTA's output rows from the
+    // producer's per-tile partials, and u / v of this column, fetched while the
+    // MMAs run (published by the barrier before the push).
+    __shared__ float ln_ms[64][2];
+    float un = 0.f, vn = 0.f;
+    if constexpr (kFuse) {
+      if (p.ln_stats) {
+        if ((int)threadIdx.x < r_cnt && r_lo + (int)threadIdx.x < p.M) {
+          const int m = r_lo + threadIdx.x;
+          float s1 = 0.f, s2 = 0.f;
+          for (int q = 0; q < p.ln_parts; ++q) {
+            s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
+            s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
+          }
+          const float mean = s1 * p.ln_inv_k;
+          ln_ms[threadIdx.x][0] = mean;
+          ln_ms[threadIdx.x][1] = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
+        }
+        if (n_ok) {
+          un = p.ln_u[n];
+          vn = p.ln_v[n];
+        }
       }
     }
     const bool ok = mbar_wait(smem_addr(done), 0);
@@ -272,53 +348,93 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     // reading its source: no CTA leaves while a peer still copies from it.
     cluster_arrive();
     if (r_cnt > 0) {
+      // Fused extras: output row statistics, KV append.
+      __shared__ float st_red[kSkThreads / 32][64][2];
+      int64_t kv_pos = 0;
+      __nv_bfloat16* kv_dst = nullptr;
+      if constexpr (kFuse) {
+        if (p.kc && n_ok && n >= p.kv_C) {
+          const int idx = n - p.kv_C;
+          const int which = idx / p.kv_C, hd = idx - which * p.kv_C;
+          const int h = hd / p.kv_D, d = hd - h * p.kv_D;
+          kv_pos = p.kv_pos0 + (p.kv_pos ? *p.kv_pos : 0);
+          kv_dst = (which == 0 ? p.kc : p.vc) + ((int64_t)h * p.kv_tmax + kv_pos) * p.kv_D + d;
+        }
+      }
       // thread nl: column n, rows r_lo .. r_lo + r_cnt; fixed summation order.
       auto finish = [&](int j0, const float4& acc, const float* radd) {
         const float o4[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int m = r_lo + j0 + e;
+          float yf = 0.f;
           if (m < p.M && n_ok) {
-            float x = o4[e] + bcol;
+            float x = o4[e];
+            if (kFuse && p.ln_stats) x = ln_ms[j0 + e][1] * (x - ln_ms[j0 + e][0] * un) + vn;
+            else x += bcol;
             if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
             if (EPI == GPT_EPI_BIAS_RESIDUAL) x += radd[e];
-            p.C[(int64_t)m * p.ldc + n] = __float2bfloat16_rn(x);
+            const __nv_bfloat16 y = __float2bfloat16_rn(x);
+            p.C[(int64_t)m * p.ldc + n] = y;
+            yf = __bfloat162float(y);
+            if (kFuse && kv_dst) {
+              if (kv_pos < p.kv_tmax) kv_dst[(int64_t)m * p.kv_H * p.kv_tmax * p.kv_D] = y;
+              else if (nl == 0) record_device_error(GPT_DEVERR_INDEX);
+            }
+          }
+          if (kFuse && p.stats_out && m < p.M) {  // m < M is uniform across the CTA
+            const float a = warp_sum(yf), b = warp_sum(yf * yf);
+            if (lane == 0) {
+              st_red[warp][j0 + e][0] = a;
+              st_red[warp][j0 + e][1] = b;
+            }
           }
         }
       };
       auto reduce4 = [&](int j0) {
-        // slot [sidx][j][128]: lane == column, conflict-free. All slots are
-        // read before the first add (no load-use chain across peers).
-        float v[kSkMaxSplits][4];
-#pragma unroll
-        for (int sidx = 0; sidx < kSkMaxSplits; ++sidx) {
-          if (sidx < p.splits) {
-            const float* bs = recv + (sidx * p.rows_per + j0) * 128 + nl;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) v[sidx][e] = bs[e * 128];
-          }
+        // slot [sidx][j][128]: lane == column, conflict-free; a runtime loop
+        // over the peers keeps this epilogue small (instruction cache).
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+        for (int sidx = 0; sidx < p.splits; ++sidx) {
+          const float* bs = recv + (sidx * p.rows_per + j0) * 128 + nl;
+          acc.x += bs[0];
+          acc.y += bs[128];
+          acc.z += bs[256];
+          acc.w += bs[384];
         }
-        float4 acc = make_float4(v[0][0], v[0][1], v[0][2], v[0][3]);
-#pragma unroll
-        for (int sidx = 1; sidx < kSkMaxSplits; ++sidx)
-          if (sidx < p.splits) {
-            acc.x += v[sidx][0]; acc.y += v[sidx][1]; acc.z += v[sidx][2]; acc.w += v[sidx][3];
-          }
         return acc;
       };
       if (got) {
-#pragma unroll
-        for (int j0 = 0; j0 < kMaxPre; j0 += 4)
-          if (j0 < r_cnt) finish(j0, reduce4(j0), &rpre[j0]);
-        for (int j0 = kMaxPre; j0 < r_cnt; j0 += 4) {
+#pragma unroll 1
+        for (int j0 = 0; j0 < r_cnt; j0 += 4) {
           float radd[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int m = r_lo + j0 + e;
-            radd[e] = (EPI == GPT_EPI_BIAS_RESIDUAL && m < p.M && n_ok)
-                          ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+            if (j0 == 0) {
+              radd[e] = rpre[e];
+            } else {
+              radd[e] = (EPI == GPT_EPI_BIAS_RESIDUAL && m < p.M && n_ok)
+                            ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+            }
           }
           finish(j0, reduce4(j0), radd);
+        }
+      }
+      if (kFuse && p.stats_out) {
+        __syncthreads();
+        const int j = threadIdx.x;
+        if (j < r_cnt && r_lo + j < p.M) {
+          float a = 0.f, b = 0.f;
+#pragma unroll
+          for (int w = 0; w < kSkThreads / 32; ++w) {
+            a += st_red[w][j][0];
+            b += st_red[w][j][1];
+          }
+          float* dst = p.stats_out + ((int64_t)tile * p.M + r_lo + j) * 2;
+          dst[0] = a;
+          dst[1] = b;
         }
       }
     }
@@ -342,7 +458,8 @@ struct SkPlan {
 // limit, never an empty K slice. Each cluster CTA then reduces rows_per output rows
 // (a power of two, at least 4, splits x rows_per >= Mp); the ring gets as
 // many stages as fit beside the receive buffer.
-inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits) {
+inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits, int min_splits = 1,
+                      int max_rows_per = kSkMaxM) {
   SkPlan pl;
   pl.Mp = (int)(((M + 15) / 16) * 16);
   pl.tiles = (int)((N + 127) / 128);
@@ -356,6 +473,9 @@ inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits) 
     return e ? atoi(e) : 0;
   }();
   if (forced > 0) want = forced;
+  const int min_rows = (pl.Mp + max_rows_per - 1) / max_rows_per;
+  if (want < min_splits) want = min_splits;
+  if (want < min_rows) want = min_rows;
   if (want > max_splits) want = max_splits;
   if (want > pl.nkb) want = pl.nkb;
   if (want < 1) want = 1;
@@ -372,10 +492,10 @@ inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits) 
   return pl;
 }
 
-template <int EPI>
+template <int EPI, bool kFuse>
 static int sk_launch(const CUtensorMap& tw, const CUtensorMap& ta, const SkParams& p, int tiles, int smem,
                      cudaStream_t st) {
-  auto kern = gemm_skinny_kernel<EPI>;
+  auto kern = gemm_skinny_kernel<EPI, kFuse>;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)tiles, (unsigned)p.splits, 1);
   cfg.blockDim = dim3(kSkThreads, 1, 1);
@@ -397,7 +517,7 @@ static int sk_launch(const CUtensorMap& tw, const CUtensorMap& ta, const SkParam
 
 // Largest cluster this kernel may use on the current device (8 portable,
 // 16 where the non-portable attribute is accepted); set up once per device.
-template <int EPI>
+template <int EPI, bool kFuse>
 static int sk_setup(int* max_splits) {
   static int cached[64] = {0};
   static std::mutex mu;
@@ -406,9 +526,8 @@ static int sk_setup(int* max_splits) {
   if (dev < 0 || dev >= 64) return fail(GPT_ERR_UNSUPPORTED, "device %d", dev);
   std::lock_guard<std::mutex> g(mu);
   if (cached[dev] == 0) {
-    auto kern = gemm_skinny_kernel<EPI>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           kSkSmemLimit);
+    auto kern = gemm_skinny_kernel<EPI, kFuse>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSkSmemLimit);
     if (e != cudaSuccess) return fail(GPT_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     // Clusters above 8 CTAs are non-portable; they are used only when the
     // attribute is accepted and a 16-CTA cluster of the largest footprint fits.
@@ -435,15 +554,20 @@ static int sk_setup(int* max_splits) {
   return GPT_OK;
 }
 
-template <int EPI>
+template <int EPI, bool kFuse>
 static int gemm_skinny_epi(const void* A, int64_t lda, const void* W, const SkParams& p0, int64_t M, int64_t N,
                            int64_t K, cudaStream_t st) {
   int max_splits = 8;
-  int s = sk_setup<EPI>(&max_splits);
+  int s = sk_setup<EPI, kFuse>(&max_splits);
   if (s) return s;
   int sms = device_sm_count();
   if (sms <= 0) return fail(GPT_ERR_CUDA, "no CUDA device");
-  SkPlan pl = sk_plan(M, N, K, sms, max_splits);
+  // Output statistics and the KV append live in the split-K owner epilogue
+  // (at least 2 splits, at most 64 rows per owner CTA).
+  const bool owner_extras = kFuse && (p0.stats_out || p0.kc);
+  SkPlan pl = sk_plan(M, N, K, sms, max_splits, owner_extras ? 2 : 1, kFuse ? 64 : kSkMaxM);
+  if (owner_extras && pl.splits < 2)
+    return fail(GPT_ERR_UNSUPPORTED, "gpt_gemm_fused: row statistics / KV append need K >= %d", 2 * BK);
   CUtensorMap tw, ta;
   s = make_map(&tw, W, N, K, K, 128);
   if (s) return s;
@@ -456,13 +580,13 @@ static int gemm_skinny_epi(const void* A, int64_t lda, const void* W, const SkPa
   p.splits = pl.splits;
   p.stages = pl.stages;
   p.rows_per = pl.rows_per;
-  return sk_launch<EPI>(tw, ta, p, pl.tiles, sk_smem_bytes(pl.Mp, p.stages, p.splits, p.rows_per), st);
+  return sk_launch<EPI, kFuse>(tw, ta, p, pl.tiles, sk_smem_bytes(pl.Mp, p.stages, p.splits, p.rows_per), st);
 }
 
 // Serves bf16 requests with M <= kSkMaxM rows.
 int gemm_skinny(const void* A, int64_t lda, const void* W, const void* bias, const void* R, int64_t ldr, void* C,
                 int64_t ldc, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t st) {
-  SkParams p;
+  SkParams p = {};
   p.M = (int)M;
   p.N = (int)N;
   p.K = (int)K;
@@ -472,10 +596,47 @@ int gemm_skinny(const void* A, int64_t lda, const void* W, const void* bias, con
   p.ldr = ldr;
   p.ldc = ldc;
   switch (epi) {
-    case GPT_EPI_NONE: return gemm_skinny_epi<GPT_EPI_NONE>(A, lda, W, p, M, N, K, st);
-    case GPT_EPI_BIAS: return gemm_skinny_epi<GPT_EPI_BIAS>(A, lda, W, p, M, N, K, st);
-    case GPT_EPI_BIAS_GELU: return gemm_skinny_epi<GPT_EPI_BIAS_GELU>(A, lda, W, p, M, N, K, st);
-    default: return gemm_skinny_epi<GPT_EPI_BIAS_RESIDUAL>(A, lda, W, p, M, N, K, st);
+    case GPT_EPI_NONE: return gemm_skinny_epi<GPT_EPI_NONE, false>(A, lda, W, p, M, N, K, st);
+    case GPT_EPI_BIAS: return gemm_skinny_epi<GPT_EPI_BIAS, false>(A, lda, W, p, M, N, K, st);
+    case GPT_EPI_BIAS_GELU: return gemm_skinny_epi<GPT_EPI_BIAS_GELU, false>(A, lda, W, p, M, N, K, st);
+    default: return gemm_skinny_epi<GPT_EPI_BIAS_RESIDUAL, false>(A, lda, W, p, M, N, K, st);
+  }
+}
+
+// Few-row GEMM with the fused decode extras (LayerNorm fold, output row
+// statistics, KV append); the caller has validated the arguments.
+int gemm_skinny_fused(const void* A, int64_t lda, const void* W, const void* bias, const void* R, int64_t ldr,
+                      void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epi, const gpt_gemm_fusion& f,
+                      cudaStream_t st) {
+  SkParams p = {};
+  p.M = (int)M;
+  p.N = (int)N;
+  p.K = (int)K;
+  p.bias = (const __nv_bfloat16*)bias;
+  p.resid = (const __nv_bfloat16*)R;
+  p.C = (__nv_bfloat16*)C;
+  p.ldr = ldr;
+  p.ldc = ldc;
+  p.ln_stats = f.ln_stats;
+  p.ln_u = f.ln_u;
+  p.ln_v = f.ln_v;
+  p.ln_parts = (int)f.ln_parts;
+  p.ln_eps = f.ln_eps;
+  p.ln_inv_k = 1.0f / (float)K;
+  p.stats_out = f.row_stats;
+  p.kc = (__nv_bfloat16*)f.k_cache;
+  p.vc = (__nv_bfloat16*)f.v_cache;
+  p.kv_C = (int)(f.kv_heads * f.kv_dim);
+  p.kv_D = (int)f.kv_dim;
+  p.kv_H = (int)f.kv_heads;
+  p.kv_tmax = f.kv_tmax;
+  p.kv_pos0 = f.kv_pos0;
+  p.kv_pos = f.kv_pos_dev;
+  switch (epi) {
+    case GPT_EPI_NONE: return gemm_skinny_epi<GPT_EPI_NONE, true>(A, lda, W, p, M, N, K, st);
+    case GPT_EPI_BIAS: return gemm_skinny_epi<GPT_EPI_BIAS, true>(A, lda, W, p, M, N, K, st);
+    case GPT_EPI_BIAS_GELU: return gemm_skinny_epi<GPT_EPI_BIAS_GELU, true>(A, lda, W, p, M, N, K, st);
+    default: return gemm_skinny_epi<GPT_EPI_BIAS_RESIDUAL, true>(A, lda, W, p, M, N, K, st);
   }
 }
 

@@ -6,6 +6,7 @@ sibling modules (``cutile_gelu`` …) allocate their outputs and delegate here.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -75,6 +76,62 @@ def gemm(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.Tensor
     L.check(L.lib().gpt_gemm(_ptr(a), lda, _ptr(w), _ptr(bias), _ptr(resid), ldr, _ptr(out), ldc, M, N, K,
                              epilogue, L.dtype_code(a.dtype), L.stream_ptr()), "gpt_gemm")
     return out
+
+
+def gemm_fused(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.Tensor | None = None,
+               resid: torch.Tensor | None = None, epilogue: int | None = None, ln=None,
+               row_stats: torch.Tensor | None = None, kv=None) -> torch.Tensor:
+    """Few-row (decode) GEMM with fused extras, bf16, M <= 256.
+
+    ln = (stats [parts, M, 2] fp32, eps, u [N] fp32, v [N] fp32): LayerNorm folded in, `w` being the
+    gamma-scaled weight from lnfold_weights; row_stats [ceil(N/128), M, 2] fp32 receives the
+    per-tile (sum, sum of squares) of the stored rows; kv = (k_cache, v_cache [B, H, Tmax, D],
+    pos_dev int64 [1] or None, pos0) appends the k / v parts of a fused QKV output.
+    """
+    M, K = a.shape
+    N = w.shape[0]
+    if w.shape[1] != K or not w.is_contiguous():
+        raise ValueError(f"gemm_fused: weight must be a contiguous [N, K={K}] tensor, got {tuple(w.shape)}")
+    if epilogue is None:
+        epilogue = (L.EPI_NONE if bias is None and ln is None else
+                    L.EPI_BIAS if resid is None else L.EPI_BIAS_RESIDUAL)
+    f = L.GemmFusion()
+    if ln is not None:
+        stats, eps, u, v = ln
+        f.ln_stats, f.ln_parts, f.ln_eps, f.ln_u, f.ln_v = _ptr(stats), stats.shape[0], float(eps), _ptr(u), _ptr(v)
+    if row_stats is not None:
+        f.row_stats = _ptr(row_stats)
+    if kv is not None:
+        kc, vc, pos_dev, pos0 = kv
+        _, H, Tmax, D = kc.shape
+        f.k_cache, f.v_cache, f.kv_heads, f.kv_dim, f.kv_tmax = _ptr(kc), _ptr(vc), H, D, Tmax
+        f.kv_pos0, f.kv_pos_dev = int(pos0), _ptr(pos_dev)
+    lda = _row_stride(a, "gemm A")
+    ldc = _row_stride(out, "gemm C")
+    ldr = _row_stride(resid, "gemm residual") if resid is not None else 0
+    L.check(L.lib().gpt_gemm_fused(_ptr(a), lda, _ptr(w), _ptr(bias), _ptr(resid), ldr, _ptr(out), ldc, M, N, K,
+                                   epilogue, ctypes.byref(f), L.dtype_code(a.dtype), L.stream_ptr()),
+            "gpt_gemm_fused")
+    return out
+
+
+def row_stats(x: torch.Tensor, stats: torch.Tensor) -> torch.Tensor:
+    """stats [1, M, 2] fp32 <- (sum, sum of squares) of each row of x [M, C]."""
+    M, C = x.shape
+    L.check(L.lib().gpt_row_stats(_ptr(x), _row_stride(x, "row_stats"), M, C, _ptr(stats), L.dtype_code(x.dtype),
+                                  L.stream_ptr()), "gpt_row_stats")
+    return stats
+
+
+def lnfold_weights(w: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, bias: torch.Tensor | None):
+    """LayerNorm fold of Linear w [N, K]: (w * gamma, u [N] fp32, v [N] fp32), see gpt_lnfold_weights."""
+    N, K = w.shape
+    wf = torch.empty_like(w)
+    u = torch.empty(N, dtype=torch.float32, device=w.device)
+    v = torch.empty(N, dtype=torch.float32, device=w.device)
+    L.check(L.lib().gpt_lnfold_weights(_ptr(w), _ptr(gamma), _ptr(beta), _ptr(bias), N, K, _ptr(wf), _ptr(u),
+                                       _ptr(v), L.dtype_code(w.dtype), L.stream_ptr()), "gpt_lnfold_weights")
+    return wf, u, v
 
 
 def attention_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor,

@@ -53,7 +53,7 @@ class _Workspace:
 class _DecodeState:
     """Buffers of the KV-cache generation loop for one (B, Tmax)."""
 
-    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device, fused: bool = True):
+    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device, fused: bool = True, fold: bool = True):
         C, H = cfg.n_embd, cfg.n_head
         D = C // H
         self.B, self.Tmax = B, Tmax
@@ -74,6 +74,13 @@ class _DecodeState:
         self.seed = torch.zeros((1,), dtype=torch.int64, device=device)   # RNG seed of the sampling kernel
         # fused decode step (one persistent kernel for all blocks), when the shapes allow it
         self.fused = (fused and dtype == torch.bfloat16 and D == 64 and C % 128 == 0 and C <= 2048 and 1 <= B <= 64)
+        # folded decode step: bf16, up to 128 rows (the split-K receive buffers of the fused GEMMs
+        # fit shared memory up to there), 16-byte row pitches for the TMA operands
+        self.fold = (fold and not self.fused and dtype == torch.bfloat16 and 1 <= B <= 128 and C % 8 == 0
+                     and cfg.n_layer >= 1)
+        if self.fold:
+            parts = (C + 127) // 128
+            self.stats = torch.zeros((2 * cfg.n_layer + 1, parts, B, 2), dtype=torch.float32, device=device)
         if self.fused:
             self.fused_ws = torch.zeros((ops.decode_fused_workspace_bytes(B, C),), dtype=torch.uint8, device=device)
             self.fused_plan = None   # built from the model's weights on first use
@@ -98,6 +105,12 @@ class CutileGPT:
         # Single-kernel fused decode step (opt-in, GPT_DECODE_FUSED=1): correct and tested, but on
         # B200 at B=64 it is still slower than the per-op step (0.90 vs 0.77 ms per GPT-2 124M step).
         self.fused_decode = os.environ.get("GPT_DECODE_FUSED", "0") == "1"
+        # Folded decode step (opt-in, GPT_DECODE_FOLD=1; bf16, up to 128 sequences): ln_1 / ln_2 /
+        # ln_f folded into the following GEMMs (row statistics produced by the residual GEMMs'
+        # epilogues) and the KV append fused into the QKV GEMM. Correct and tested; on B200 at B=64
+        # it is still slower than the per-op step (0.61 vs 0.56 ms per GPT-2 124M step).
+        self.fold_decode = os.environ.get("GPT_DECODE_FOLD", "0") == "1"
+        self._folded: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]] = None
         self._init_weights(seed)
 
     # ------------------------------------------------------------------ weights
@@ -131,6 +144,7 @@ class CutileGPT:
             device=self.device, dtype=self.dtype).contiguous()
         self.weights = conv
         self._dec.clear()
+        self._folded = None
 
     def _check_shapes(self, state):
         cfg = self.config
@@ -246,9 +260,28 @@ class CutileGPT:
         if st is None:
             if len(self._dec) >= 2:
                 self._dec.pop(next(iter(self._dec)))
-            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device, fused=self.fused_decode)
+            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device, fused=self.fused_decode,
+                              fold=self.fold_decode)
             self._dec[key] = st
+        if st.fold:
+            self._fold_weights()   # eager, outside any graph capture
         return st
+
+    def _fold_weights(self) -> Dict[str, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]:
+        """(gamma-scaled weight, u, v) of every Linear that follows a LayerNorm (see ops.lnfold_weights)."""
+        if self._folded is None:
+            cfg = self.config
+            f = {}
+            for i in range(cfg.n_layer):
+                p = f'h.{i}.'
+                f[p + 'attn'] = ops.lnfold_weights(self._w(p + 'attn.c_attn.weight'), self._w(p + 'ln_1.weight'),
+                                                   self._w(p + 'ln_1.bias'), self._w(p + 'attn.c_attn.bias'))
+                f[p + 'fc'] = ops.lnfold_weights(self._w(p + 'mlp.c_fc.weight'), self._w(p + 'ln_2.weight'),
+                                                 self._w(p + 'ln_2.bias'), self._w(p + 'mlp.c_fc.bias'))
+            f['lm'] = ops.lnfold_weights(self._w('lm_head.weight'), self._w('ln_f.weight'), self._w('ln_f.bias'),
+                                         None)
+            self._folded = f
+        return self._folded
 
     def _decode_step(self, st: _DecodeState) -> None:
         """One token per sequence at device position *st.pos: logits into st.logits."""
@@ -265,6 +298,31 @@ class CutileGPT:
         B = st.B
         ops.embedding_pos(st.tok.view(B, 1), self._w('wte'), self._w('wpe'), st.x, pos0=0, pos_dev=st.pos)
         q = st.qkv[:, :C]
+        if st.fold:
+            # LayerNorms folded into the GEMMs that follow them; statistics slot 2i holds the rows
+            # entering block i (parts: 1 from the embedding, then one per 128-column tile of the
+            # residual GEMMs), slot 2i+1 the rows after its attention.
+            F = self._fold_weights()
+            eps = 1e-5
+            ops.row_stats(st.x, st.stats[0, :1])
+            for i in range(cfg.n_layer):
+                p = f'h.{i}.'
+                s_in = st.stats[2 * i, :1] if i == 0 else st.stats[2 * i]
+                wf, u, v = F[p + 'attn']
+                ops.gemm_fused(st.x, wf, st.qkv, epilogue=L.EPI_BIAS, ln=(s_in, eps, u, v),
+                               kv=(st.cache[i, 0], st.cache[i, 1], st.pos, 0))
+                ops.attention_decode(q, st.cache[i, 0], st.cache[i, 1], st.att, 1, st.dec_ws, scale,
+                                     len_dev=st.pos)
+                ops.gemm_fused(st.att, self._w(p + 'attn.c_proj.weight'), st.x, bias=self._w(p + 'attn.c_proj.bias'),
+                               resid=st.x, row_stats=st.stats[2 * i + 1])
+                wf, u, v = F[p + 'fc']
+                ops.gemm_fused(st.x, wf, st.f, epilogue=L.EPI_BIAS_GELU, ln=(st.stats[2 * i + 1], eps, u, v))
+                ops.gemm_fused(st.f, self._w(p + 'mlp.c_proj.weight'), st.x, bias=self._w(p + 'mlp.c_proj.bias'),
+                               resid=st.x, row_stats=st.stats[2 * i + 2])
+            wf, u, v = F['lm']
+            s_in = st.stats[2 * cfg.n_layer, :1] if cfg.n_layer == 0 else st.stats[2 * cfg.n_layer]
+            ops.gemm_fused(st.x, wf, st.logits, epilogue=L.EPI_NONE, ln=(s_in, eps, u, v))
+            return
         for i in range(cfg.n_layer):
             p = f'h.{i}.'
             ops.layernorm(st.x, self._w(p + 'ln_1.weight'), self._w(p + 'ln_1.bias'), st.h)

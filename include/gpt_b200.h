@@ -204,6 +204,57 @@ GPT_API int gpt_decode_advance(const int64_t* tok, int64_t B, int64_t* seq,
 GPT_API int gpt_argmax(const void* logits, int64_t ld, int64_t B, int64_t V,
                int64_t* out, int dtype, void* stream);
 
+/* ---- fused decode GEMM (few rows: M <= 256, bf16) ---------------------
+ * Optional extras of gpt_gemm for the KV-cache decode step; every pointer may
+ * be NULL (extra off).
+ *  - LayerNorm folded into the GEMM (replaces ln_1 / ln_2 / ln_f + GEMM of
+ *    cutile_gpt/models/gpt.py:121-130, :158-167, :177-181): A holds the raw
+ *    rows x, W the gamma-scaled weight W' = W * gamma (gpt_lnfold_weights),
+ *    C = rstd * (x W'^T - mean * ln_u) + ln_v (+ GELU), with mean / rstd of
+ *    each row of x from ln_stats [ln_parts][M][2] (sum, sum of squares),
+ *    var = E[x^2] - mean^2 as cutile_gpt/kernels/layernorm.py:58-62, and
+ *    ln_eps. The bias argument is unused (ln_v holds W . beta + bias).
+ *  - row_stats: per 128-column tile, the (sum, sum of squares) of every
+ *    stored output row -> row_stats [ceil(N / 128)][M][2]: the ln_stats of
+ *    the next folded GEMM (residual stream after attn c_proj / mlp c_proj).
+ *  - k_cache / v_cache: the output is the fused QKV row [q | k | v] of
+ *    kv_heads x kv_dim each; its k and v parts are also written to the caches
+ *    [M][kv_heads][kv_tmax][kv_dim] at position kv_pos0 + *kv_pos_dev
+ *    (replaces gpt_kv_append). */
+typedef struct gpt_gemm_fusion {
+  const float* ln_stats;
+  int64_t ln_parts;
+  float ln_eps;
+  const float* ln_u;
+  const float* ln_v;
+  float* row_stats;
+  void* k_cache;
+  void* v_cache;
+  int64_t kv_heads;
+  int64_t kv_dim;
+  int64_t kv_tmax;
+  int64_t kv_pos0;
+  const int64_t* kv_pos_dev;
+} gpt_gemm_fusion;
+
+GPT_API int gpt_gemm_fused(const void* A, int64_t lda, const void* W,
+               const void* bias, const void* R, int64_t ldr, void* C,
+               int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue,
+               const gpt_gemm_fusion* fusion, int dtype, void* stream);
+
+/* (sum, sum of squares) of each row of x [M, C] (row stride ld) ->
+ * stats [1][M][2]: the ln_stats of a folded GEMM that reads the embedding
+ * output directly. */
+GPT_API int gpt_row_stats(const void* x, int64_t ld, int64_t M, int64_t C,
+               float* stats, int dtype, void* stream);
+
+/* LayerNorm fold of a Linear [N, K] that follows LayerNorm(gamma, beta):
+ * Wf = W * gamma (per input column, rounded to dtype), u[n] = sum_k Wf[n,k],
+ * v[n] = sum_k W[n,k] * beta[k] + bias[n] (bias may be NULL), u / v fp32. */
+GPT_API int gpt_lnfold_weights(const void* W, const void* gamma,
+               const void* beta, const void* bias, int64_t N, int64_t K,
+               void* Wf, float* u, float* v, int dtype, void* stream);
+
 /* Sampling step of generate() with temperature / top_k
  * (cutile_gpt/models/gpt.py:207-225: logits / temperature, top-k mask of
  * values below the k-th largest, softmax, multinomial draw), one launch for

@@ -385,3 +385,75 @@ def test_sample_edges():
     assert seen0 == {3, 10, 11}
     with pytest.raises(Exception):
         ops.sample(x.cuda(), out, 0.0, None)
+
+
+# ----------------------------------------------------------------- fused decode GEMM (LayerNorm fold, row stats, KV)
+@pytest.mark.parametrize("M,C,N,epi", [(64, 768, 2304, L.EPI_BIAS), (64, 768, 3072, L.EPI_BIAS_GELU),
+                                       (5, 768, 50257, L.EPI_NONE), (130, 1600, 4800, L.EPI_BIAS),
+                                       (16, 384, 1536, L.EPI_BIAS_GELU)])
+def test_gemm_layernorm_fold(M, C, N, epi):
+    """ln_f/ln_1/ln_2 folded into the next GEMM equals LayerNorm then Linear (oracle in fp64)."""
+    dt = torch.bfloat16
+    x = (randn(M, C, seed=70, scale=2.0) + 0.7).to(dt)           # rows with a nonzero mean
+    g = (randn(C, seed=71) * 0.2 + 1.0).to(dt)
+    b = (randn(C, seed=72) * 0.2).to(dt)
+    w = (randn(N, C, seed=73) / math.sqrt(C)).to(dt)
+    bias = randn(N, seed=74).to(dt) if epi != L.EPI_NONE else None
+    xc, wc = x.cuda(), w.cuda()
+    wf, u, v = ops.lnfold_weights(wc, g.cuda(), b.cuda(), bias.cuda() if bias is not None else None)
+    stats = torch.empty((1, M, 2), dtype=torch.float32, device="cuda")
+    ops.row_stats(xc, stats)
+    out = torch.empty((M, N), dtype=dt, device="cuda")
+    ops.gemm_fused(xc, wf, out, epilogue=epi, ln=(stats, 1e-5, u, v))
+    h = R.layer_norm(x.double(), g.double(), b.double())
+    ref = h @ w.double().t()
+    if bias is not None:
+        ref = ref + bias.double()
+    if epi == L.EPI_BIAS_GELU:
+        ref = R.gelu(ref)
+    assert rel_err(out, ref) < BF16_REL, rel_err(out, ref)
+    s = x.double().sum(-1), (x.double() ** 2).sum(-1)
+    torch.testing.assert_close(stats[0].cpu().double(), torch.stack(s, -1), rtol=1e-5, atol=1e-3)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 768, 768), (64, 768, 3072), (120, 1600, 6400), (7, 768, 3072)])
+def test_gemm_row_stats_of_residual_output(M, N, K):
+    dt = torch.bfloat16
+    a, w = randn(M, K, seed=75).to(dt).cuda(), (randn(N, K, seed=76) / math.sqrt(K)).to(dt).cuda()
+    bias, r = randn(N, seed=77).to(dt).cuda(), randn(M, N, seed=78).to(dt).cuda()
+    parts = (N + 127) // 128
+    st = torch.full((parts, M, 2), float("nan"), dtype=torch.float32, device="cuda")
+    out = torch.empty((M, N), dtype=dt, device="cuda")
+    ops.gemm_fused(a, w, out, bias=bias, resid=r, row_stats=st)
+    ref = a.double().cpu() @ w.double().cpu().t() + bias.double().cpu() + r.double().cpu()
+    assert rel_err(out, ref) < BF16_REL
+    o = out.double().cpu()                                          # stats are of the stored bf16 rows
+    got = st.double().cpu().sum(0)
+    torch.testing.assert_close(got[:, 0], o.sum(-1), rtol=1e-5, atol=1e-2)
+    torch.testing.assert_close(got[:, 1], (o ** 2).sum(-1), rtol=1e-5, atol=1e-2)
+    for t in range(parts):                                          # each tile covers its own columns
+        seg = o[:, t * 128:(t + 1) * 128]
+        torch.testing.assert_close(st[t, :, 0].double().cpu(), seg.sum(-1), rtol=1e-5, atol=1e-2)
+
+
+@pytest.mark.parametrize("B,H", [(64, 12), (3, 25)])
+def test_gemm_qkv_kv_append(B, H):
+    """The QKV GEMM writes q|k|v and appends k, v to the caches at the device position."""
+    dt, D, Tmax = torch.bfloat16, 64, 40
+    C = H * D
+    x, w = randn(B, C, seed=79).to(dt).cuda(), (randn(3 * C, C, seed=80) / math.sqrt(C)).to(dt).cuda()
+    bias = randn(3 * C, seed=81).to(dt).cuda()
+    kc = torch.zeros((B, H, Tmax, D), dtype=dt, device="cuda")
+    vc = torch.zeros_like(kc)
+    pos = torch.tensor([17], dtype=torch.int64, device="cuda")
+    qkv = torch.empty((B, 3 * C), dtype=dt, device="cuda")
+    ops.gemm_fused(x, w, qkv, bias=bias, kv=(kc, vc, pos, 2))
+    ref = x.double().cpu() @ w.double().cpu().t() + bias.double().cpu()
+    assert rel_err(qkv, ref) < BF16_REL
+    q3 = qkv.view(B, 3, H, D).cpu()
+    assert torch.equal(kc[:, :, 19].cpu(), q3[:, 1]) and torch.equal(vc[:, :, 19].cpu(), q3[:, 2])
+    kc[:, :, 19] = 0
+    vc[:, :, 19] = 0
+    assert kc.abs().sum().item() == 0 and vc.abs().sum().item() == 0   # nothing else touched
+    with pytest.raises(ValueError):
+        ops.gemm_fused(x, w[:100], qkv[:, :100], bias=bias[:100], kv=(kc, vc, pos, 0))   # N != 3 * H * D
