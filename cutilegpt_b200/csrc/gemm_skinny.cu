@@ -29,6 +29,7 @@ struct SkParams {
   int nkb, kb_per, splits;
   int stages;  // ring depth: at most kSkStages and the k-blocks per CTA
   int rows_per;  // split-K: output rows reduced (and stored) by each cluster CTA, a power of two >= 4
+  int vec_c;     // C rows allow 8-byte stores (16-bit elements, pitch and base multiples of 4 elements)
   const __nv_bfloat16* bias;
   const __nv_bfloat16* resid;
   __nv_bfloat16* C;
@@ -273,42 +274,49 @@ __global__ void __launch_bounds__(kSkThreads, 4)
       }
     }
   } else {
-    // Bias and residual of this CTA's output rows are fetched while the
-    // partials are still being produced.
-    constexpr int kMaxPre = 4;  // residual rows fetched ahead (the first group of four)
-    float bcol = 0.f;
-    // (with the LayerNorm fold the bias is part of ln_v and the pointer may be null)
-    if (EPI != GPT_EPI_NONE && n_ok && !(kFuse && p.ln_stats)) bcol = __bfloat162float(p.bias[n]);
-    float rpre[kMaxPre];
-    if (EPI == GPT_EPI_BIAS_RESIDUAL) {
+    // Owner epilogue mapping: thread = (row group rs, column group q): rows
+    // r_lo + rs, +4, ... and the 4 columns n0 + 4q .. +3, so one warp covers a
+    // whole 128-column row segment (float4 reads of the partials, 8-byte
+    // stores, row statistics by one warp reduction).
+    const int q4 = threadIdx.x & 31;
+    const int rs = threadIdx.x >> 5;
+    const int nq = n0 + 4 * q4;
+    const int ncnt = max(0, min(4, p.N - nq));  // valid columns of this group
+    // Bias (or the LayerNorm fold's u / v) of these columns, and the residual
+    // of the first row, fetched while the partials are still being produced.
+    float b4[4] = {0.f, 0.f, 0.f, 0.f}, u4[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool ln = kFuse && p.ln_stats != nullptr;
 #pragma unroll
-      for (int j = 0; j < kMaxPre; ++j) {
-        const int m = r_lo + j;
-        rpre[j] = (j < r_cnt && m < p.M && n_ok) ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+    for (int e = 0; e < 4; ++e) {
+      if (e < ncnt) {
+        if (ln) {
+          u4[e] = p.ln_u[nq + e];
+          b4[e] = p.ln_v[nq + e];
+        } else if (EPI != GPT_EPI_NONE) {
+          b4[e] = __bfloat162float(p.bias[nq + e]);
+        }
       }
     }
+    float rpre[4] = {0.f, 0.f, 0.f, 0.f};
+    if (EPI == GPT_EPI_BIAS_RESIDUAL && rs < r_cnt && r_lo + rs < p.M) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (e < ncnt) rpre[e] = __bfloat162float(p.resid[(int64_t)(r_lo + rs) * p.ldr + nq + e]);
+    }
     // LayerNorm fold: mean / rstd of this CTA's output rows from the
-    // producer's per-tile partials, and u / v of this column, fetched while the
-    // MMAs run (published by the barrier before the push).
+    // producer's per-tile partials (published by the barrier before the push).
     __shared__ float ln_ms[64][2];
-    float un = 0.f, vn = 0.f;
     if constexpr (kFuse) {
-      if (p.ln_stats) {
-        if ((int)threadIdx.x < r_cnt && r_lo + (int)threadIdx.x < p.M) {
-          const int m = r_lo + threadIdx.x;
-          float s1 = 0.f, s2 = 0.f;
-          for (int q = 0; q < p.ln_parts; ++q) {
-            s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
-            s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
-          }
-          const float mean = s1 * p.ln_inv_k;
-          ln_ms[threadIdx.x][0] = mean;
-          ln_ms[threadIdx.x][1] = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
+      if (ln && (int)threadIdx.x < r_cnt && r_lo + (int)threadIdx.x < p.M) {
+        const int m = r_lo + threadIdx.x;
+        float s1 = 0.f, s2 = 0.f;
+        for (int q = 0; q < p.ln_parts; ++q) {
+          s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
+          s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
         }
-        if (n_ok) {
-          un = p.ln_u[n];
-          vn = p.ln_v[n];
-        }
+        const float mean = s1 * p.ln_inv_k;
+        ln_ms[threadIdx.x][0] = mean;
+        ln_ms[threadIdx.x][1] = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
       }
     }
     const bool ok = mbar_wait(smem_addr(done), 0);
@@ -344,97 +352,89 @@ __global__ void __launch_bounds__(kSkThreads, 4)
       got = mbar_wait(smem_addr(recv_full), 0);
       SK_STAMP(5);
     }
+    got = __all_sync(0xffffffffu, got);  // warp-uniform: the row statistics use full-warp shuffles
     // Every owner has received its rows, so every bulk copy has finished
     // reading its source: no CTA leaves while a peer still copies from it.
     cluster_arrive();
-    if (r_cnt > 0) {
-      // Fused extras: output row statistics, KV append.
-      __shared__ float st_red[kSkThreads / 32][64][2];
-      int64_t kv_pos = 0;
+    if (r_cnt > 0 && got) {
+      // KV append target of this column group (k or v part of a fused QKV row;
+      // 4 | head_dim keeps the group inside one head).
       __nv_bfloat16* kv_dst = nullptr;
       if constexpr (kFuse) {
-        if (p.kc && n_ok && n >= p.kv_C) {
-          const int idx = n - p.kv_C;
+        if (p.kc && ncnt > 0 && nq >= p.kv_C) {
+          const int idx = nq - p.kv_C;
           const int which = idx / p.kv_C, hd = idx - which * p.kv_C;
           const int h = hd / p.kv_D, d = hd - h * p.kv_D;
-          kv_pos = p.kv_pos0 + (p.kv_pos ? *p.kv_pos : 0);
-          kv_dst = (which == 0 ? p.kc : p.vc) + ((int64_t)h * p.kv_tmax + kv_pos) * p.kv_D + d;
+          const int64_t kv_pos = p.kv_pos0 + (p.kv_pos ? *p.kv_pos : 0);
+          if (kv_pos < p.kv_tmax)
+            kv_dst = (which == 0 ? p.kc : p.vc) + ((int64_t)h * p.kv_tmax + kv_pos) * p.kv_D + d;
+          else if (q4 == 0 && rs == 0)
+            record_device_error(GPT_DEVERR_INDEX);
         }
       }
-      // thread nl: column n, rows r_lo .. r_lo + r_cnt; fixed summation order.
-      auto finish = [&](int j0, const float4& acc, const float* radd) {
-        const float o4[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int m = r_lo + j0 + e;
-          float yf = 0.f;
-          if (m < p.M && n_ok) {
-            float x = o4[e];
-            if (kFuse && p.ln_stats) x = ln_ms[j0 + e][1] * (x - ln_ms[j0 + e][0] * un) + vn;
-            else x += bcol;
-            if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
-            if (EPI == GPT_EPI_BIAS_RESIDUAL) x += radd[e];
-            const __nv_bfloat16 y = __float2bfloat16_rn(x);
-            p.C[(int64_t)m * p.ldc + n] = y;
-            yf = __bfloat162float(y);
-            if (kFuse && kv_dst) {
-              if (kv_pos < p.kv_tmax) kv_dst[(int64_t)m * p.kv_H * p.kv_tmax * p.kv_D] = y;
-              else if (nl == 0) record_device_error(GPT_DEVERR_INDEX);
-            }
-          }
-          if (kFuse && p.stats_out && m < p.M) {  // m < M is uniform across the CTA
-            const float a = warp_sum(yf), b = warp_sum(yf * yf);
-            if (lane == 0) {
-              st_red[warp][j0 + e][0] = a;
-              st_red[warp][j0 + e][1] = b;
-            }
-          }
-        }
-      };
-      auto reduce4 = [&](int j0) {
-        // slot [sidx][j][128]: lane == column, conflict-free; a runtime loop
-        // over the peers keeps this epilogue small (instruction cache).
+      const bool vec_c = p.vec_c && ncnt == 4;
+#pragma unroll 1
+      for (int j = rs; j < r_cnt; j += kSkThreads / 32) {   // warp-uniform
+        const int m = r_lo + j;
+        if (m >= p.M) break;
+        // fixed summation order over the peers (peer 0 first)
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 4
         for (int sidx = 0; sidx < p.splits; ++sidx) {
-          const float* bs = recv + (sidx * p.rows_per + j0) * 128 + nl;
-          acc.x += bs[0];
-          acc.y += bs[128];
-          acc.z += bs[256];
-          acc.w += bs[384];
+          const float4 v = *reinterpret_cast<const float4*>(recv + (sidx * p.rows_per + j) * 128 + 4 * q4);
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
         }
-        return acc;
-      };
-      if (got) {
-#pragma unroll 1
-        for (int j0 = 0; j0 < r_cnt; j0 += 4) {
-          float radd[4];
+        float radd[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int m = r_lo + j0 + e;
-            if (j0 == 0) {
-              radd[e] = rpre[e];
+        for (int e = 0; e < 4; ++e) {
+          radd[e] = 0.f;
+          if (EPI == GPT_EPI_BIAS_RESIDUAL && e < ncnt)
+            radd[e] = j == rs ? rpre[e] : __bfloat162float(p.resid[(int64_t)m * p.ldr + nq + e]);
+        }
+        float mean = 0.f, rstd = 1.f;
+        if (ln) {
+          mean = ln_ms[j][0];
+          rstd = ln_ms[j][1];
+        }
+        const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        __nv_bfloat16 y[4];
+        float s1 = 0.f, s2 = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float x = ln ? rstd * (a4[e] - mean * u4[e]) + b4[e] : a4[e] + b4[e];
+          if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
+          if (EPI == GPT_EPI_BIAS_RESIDUAL) x += radd[e];
+          y[e] = __float2bfloat16_rn(x);
+          const float yf = e < ncnt ? __bfloat162float(y[e]) : 0.f;
+          s1 += yf;
+          s2 = fmaf(yf, yf, s2);
+        }
+        __nv_bfloat16* dst = p.C + (int64_t)m * p.ldc + nq;
+        if (vec_c) {
+          *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(y);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            if (e < ncnt) dst[e] = y[e];
+        }
+        if constexpr (kFuse) {
+          if (kv_dst) {
+            __nv_bfloat16* kd = kv_dst + (int64_t)m * p.kv_H * p.kv_tmax * p.kv_D;
+            if (ncnt == 4) {
+              *reinterpret_cast<uint2*>(kd) = *reinterpret_cast<const uint2*>(y);
             } else {
-              radd[e] = (EPI == GPT_EPI_BIAS_RESIDUAL && m < p.M && n_ok)
-                            ? __bfloat162float(p.resid[(int64_t)m * p.ldr + n]) : 0.f;
+              for (int e = 0; e < ncnt; ++e) kd[e] = y[e];
             }
           }
-          finish(j0, reduce4(j0), radd);
-        }
-      }
-      if (kFuse && p.stats_out) {
-        __syncthreads();
-        const int j = threadIdx.x;
-        if (j < r_cnt && r_lo + j < p.M) {
-          float a = 0.f, b = 0.f;
-#pragma unroll
-          for (int w = 0; w < kSkThreads / 32; ++w) {
-            a += st_red[w][j][0];
-            b += st_red[w][j][1];
+          if (p.stats_out) {  // one warp holds the whole 128-column segment of row m
+            s1 = warp_sum(s1);
+            s2 = warp_sum(s2);
+            if (q4 == 0) {
+              float* sd = p.stats_out + ((int64_t)tile * p.M + m) * 2;
+              sd[0] = s1;
+              sd[1] = s2;
+            }
           }
-          float* dst = p.stats_out + ((int64_t)tile * p.M + r_lo + j) * 2;
-          dst[0] = a;
-          dst[1] = b;
         }
       }
     }
@@ -595,6 +595,7 @@ int gemm_skinny(const void* A, int64_t lda, const void* W, const void* bias, con
   p.C = (__nv_bfloat16*)C;
   p.ldr = ldr;
   p.ldc = ldc;
+  p.vec_c = aligned(C, 8) && ldc % 4 == 0;
   switch (epi) {
     case GPT_EPI_NONE: return gemm_skinny_epi<GPT_EPI_NONE, false>(A, lda, W, p, M, N, K, st);
     case GPT_EPI_BIAS: return gemm_skinny_epi<GPT_EPI_BIAS, false>(A, lda, W, p, M, N, K, st);
@@ -617,6 +618,7 @@ int gemm_skinny_fused(const void* A, int64_t lda, const void* W, const void* bia
   p.C = (__nv_bfloat16*)C;
   p.ldr = ldr;
   p.ldc = ldc;
+  p.vec_c = aligned(C, 8) && ldc % 4 == 0;
   p.ln_stats = f.ln_stats;
   p.ln_u = f.ln_u;
   p.ln_v = f.ln_v;
