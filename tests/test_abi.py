@@ -75,3 +75,26 @@ def test_thread_local_error_string():
     t.join()
     assert seen["s"] == b""
     assert b"dtype" in lib.gpt_last_error_string()
+
+
+def test_gemm_fusion_struct_layout_matches_header(tmp_path):
+    """ctypes GemmFusion has the field offsets and size of struct gpt_gemm_fusion (compiled with gcc)."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    from cutilegpt_b200 import _lib as L
+    fields = [f[0] for f in L.GemmFusion._fields_]
+    src = tmp_path / "layout.c"
+    hdr = HEADER
+    body = "".join(f'  printf("{f} %zu\\n", offsetof(gpt_gemm_fusion, {f}));\n' for f in fields)
+    src.write_text(f'#include <stdio.h>\n#include <stddef.h>\n#include "{hdr}"\nint main(void) {{\n{body}'
+                   f'  printf("sizeof %zu\\n", sizeof(gpt_gemm_fusion));\n  return 0;\n}}\n')
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-o", str(exe), str(src)], check=True)
+    got = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    for f in fields:
+        assert int(got[f]) == getattr(L.GemmFusion, f).offset, f
+    assert int(got["sizeof"]) == ctypes.sizeof(L.GemmFusion)
