@@ -91,9 +91,13 @@ class CutileGPT:
 
     def __init__(self, config: GPTConfig, dtype: torch.dtype = torch.float32,
                  device: Optional[torch.device | str] = None, seed: Optional[int] = None):
+        self._setup(config, dtype, torch.device(device) if device is not None else torch.device('cuda'))
+        self._init_weights(seed)
+
+    def _setup(self, config: GPTConfig, dtype: torch.dtype, device: torch.device) -> None:
         self.config = config
         self.dtype = dtype
-        self.device = torch.device(device) if device is not None else torch.device('cuda')
+        self.device = device
         self.weights: Dict[str, torch.Tensor] = {}
         # The reference caches [in, out] copies of every weight (gpt.py:83-90);
         # the tensor-core GEMM reads [out, in] directly, so this stays empty.
@@ -111,7 +115,6 @@ class CutileGPT:
         # of 9. B200, GPT-2 124M, B=64: 0.49 ms per step vs 0.54 ms for the per-op step.
         self.fold_decode = os.environ.get("GPT_DECODE_FOLD", "1") == "1"
         self._folded: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]] = None
-        self._init_weights(seed)
 
     # ------------------------------------------------------------------ weights
     def _init_weights(self, seed: Optional[int] = None):
@@ -493,6 +496,24 @@ class CutileGPT:
         hf_model = GPT2LMHeadModel.from_pretrained(model_name)
         self.load_from_state_dict(hf_model.state_dict(), layout='hf')
         print(f"Loaded weights from HuggingFace: {model_name}")
+
+    def save_packed(self, path: str) -> None:
+        """Writes config + weights in the packed on-disk format (models/packed.py): the device layout and
+        dtype as they are, the tied lm_head once, for fast replica start-up (from_packed)."""
+        from . import packed
+        tied = self.weights['lm_head.weight'] is self.weights['wte']
+        packed.save(path, self.config, self.weights, tied)
+
+    @classmethod
+    def from_packed(cls, path: str, device: Optional[torch.device | str] = None) -> 'CutileGPT':
+        """A model whose config, dtype and weights come from a packed file (no random init)."""
+        from . import packed
+        dev = torch.device(device) if device is not None else torch.device('cuda')
+        cfg, dt, w = packed.load(path, dev)
+        m = cls.__new__(cls)
+        m._setup(cfg, dt, dev)
+        m.load_state(w)
+        return m
 
     def load_from_mingpt(self, mingpt_model):
         """Loads weights from a minGPT model instance (gpt.py:306-343)."""

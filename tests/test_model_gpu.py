@@ -280,3 +280,18 @@ def test_folded_decode_step_matches_per_op_step(B):
         assert ((a - b).abs().max() / b.abs().max()).item() < 2e-2
     c1, c2 = outs[0][1], outs[1][1]
     assert ((c1 - c2).abs().max() / c2.abs().max()).item() < 2e-2
+
+
+def test_packed_weights_round_trip_on_device(tmp_path):
+    """save_packed / from_packed: same config, dtype, weights and logits; tied head stays tied."""
+    cfg = GPTConfig(n_layer=2, n_head=4, n_embd=128, vocab_size=50257, block_size=64)
+    m, _ = make(cfg, torch.bfloat16, seed=23, affine=24)
+    path = str(tmp_path / "m.cgpt")
+    m.save_packed(path)
+    m2 = CutileGPT.from_packed(path)
+    assert m2.config == cfg and m2.dtype == torch.bfloat16
+    assert m2.weights['lm_head.weight'] is m2.weights['wte']
+    idx = ids(2, 30, cfg.vocab_size, 25).cuda()
+    a, _ = m(idx)
+    b, _ = m2(idx)
+    assert torch.equal(a, b)
