@@ -163,6 +163,53 @@ def barrier(world):
 
 
 # --------------------------------------------------------------------------- ours
+def _event_ms(fn, iters=20, warm=3):
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters
+
+
+def run_extras(dev):
+    """The other BASELINE configs on one GPU (seeded synthetic inputs), for the record:
+    cfg 3' standalone tanh-GELU on a [32,512,768] bf16 N(0,1) tensor (HBM-bound: 50.3 MB per call),
+    cfg 2 (6/6/384) prefill B16xT256 in bf16 and fp32, cfg 1 (nano 3/3/48, ctx 1024) fp32 B8xT256.
+    Inputs of the GELU exceed L2 only twice over, so a 256 MB buffer is rewritten between calls."""
+    from cutilegpt_b200 import CutileGPT, GPTConfig, cutile_gelu
+    _, peak_gbs, src = load_peaks()
+    g = torch.Generator(device="cpu").manual_seed(2)
+    x = torch.randn(32, 512, 768, generator=g).to(torch.bfloat16).to(dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+
+    def gelu_once():
+        flush.zero_()
+        cutile_gelu(x)
+    t_all = _event_ms(gelu_once)
+    t_flush = _event_ms(lambda: flush.zero_())
+    t = max(t_all - t_flush, 1e-6)
+    gb = x.numel() * 2 * 2 / 1e9
+    out = {"gelu_op": {"config": "cfg3' tanh-GELU [32,512,768] bf16 N(0,1), L2 flushed between calls",
+                       "us": t * 1e3, "GB/s": gb / (t / 1e3), "frac_hbm": gb / (t / 1e3) / peak_gbs,
+                       "peak_source": src}}
+    for name, cfg, B, T, dt in (("cfg2_small_bf16", GPTConfig(n_layer=6, n_head=6, n_embd=384), 16, 256, torch.bfloat16),
+                                ("cfg2_small_fp32", GPTConfig(n_layer=6, n_head=6, n_embd=384), 16, 256, torch.float32),
+                                ("cfg1_nano_fp32", GPTConfig(n_layer=3, n_head=3, n_embd=48), 8, 256, torch.float32)):
+        m = CutileGPT(cfg, dtype=dt, device=dev, seed=0)
+        idx = torch.randint(0, cfg.vocab_size, (B, T), generator=torch.Generator().manual_seed(1)).to(dev)
+        ms = _event_ms(lambda: m(idx), iters=10)
+        out[name] = {"batch": B, "seq_len": T, "ms_per_forward": ms, "tokens_per_s": B * T / (ms / 1e3),
+                     "model_tflops": flops_per_token(cfg, T) * B * T / (ms / 1e3) / 1e12}
+        del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_decode(args, model, cfg, rank, world, dev):
     """batch 64 sharded over the ranks, prompt 128, 128 greedy KV-cache steps.
 
@@ -285,9 +332,10 @@ def run_ours(args, rank, world, local):
     e2e_value = tokens / (e2e_ms / 1e3)
     torch.cuda.empty_cache()
     dec = None if args.no_decode else run_decode(args, model, cfg, rank, world, dev)
+    extras = run_extras(dev) if (world == 1 and args.model == "gpt2" and not args.no_decode) else None
     return dict(value=value, ms=ms_max / args.steps, tokens=tokens, launches=launches, clk=clk,
                 gemm_ms=gemm_ms, gemm_launches=gemm_launches, gemm_flops=gemm_flops, e2e_value=e2e_value,
-                e2e_h2d=B * T * 8, e2e_d2h=B * cfg.vocab_size * 2, dec=dec, cfg=cfg)
+                e2e_h2d=B * T * 8, e2e_d2h=B * cfg.vocab_size * 2, dec=dec, cfg=cfg, extras=extras)
 
 
 # --------------------------------------------------------------------------- CPU
@@ -417,6 +465,7 @@ def main():
             "gpu_launches": r["launches"],
             "cpu_baseline": cpu,
             "decode": r["dec"],
+            "extras": r["extras"],
             "clocks": r["clk"],
         }
         print(json.dumps(line), flush=True)

@@ -31,8 +31,11 @@ namespace tc {
 
 constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B-swizzle row
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 8;                       // epilogue warps, TMA-store variants
 constexpr int kThreads = (2 + kEpiWarps) * 32;
+// The LSU-store epilogue (row pitch not 16-byte aligned: the lm_head's 50257)
+// is instruction-latency-bound at two warps per scheduler: it gets 16 warps.
+constexpr int epi_warps(bool tma_store) { return tma_store ? kEpiWarps : 16; }
 constexpr int kStageRowPitch = 33;  // fp32 words per staged row (bank-conflict free)
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 
@@ -171,15 +174,17 @@ __device__ __forceinline__ constexpr uint32_t idesc_bf16() {
 // each CTA's TMEM holds the accumulators of its own 128 rows, which its own
 // epilogue warps drain. All loads are plain per-CTA TMA loads (no multicast);
 // only the MMA completion (tcgen05.commit) is multicast to both CTAs.
-template <int BN, bool kPair>
+template <int BN, bool kPair, int kEW = kEpiWarps>
 struct Smem {
   static constexpr int kBRows = kPair ? BN / 2 : BN;
-  static constexpr int kStages = kPair ? 6 : (BN >= 256 ? 4 : 6);
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
+  // ring depth: what fits beside the epilogue staging (16 LSU warps stage 66 KB)
+  static constexpr int kStages = kEW > kEpiWarps ? (kStageBytes <= 32768 ? 4 : 3)
+                                                 : (kPair ? 6 : (BN >= 256 ? 4 : 6));
   static constexpr int kRingBytes = kStages * kStageBytes;
-  static constexpr int kEpiBytes = kEpiWarps * 32 * kStageRowPitch * 4;
+  static constexpr int kEpiBytes = kEW * 32 * kStageRowPitch * 4;
   static constexpr int kBarBytes = (2 * kStages + 4) * 8 + 16;
   static constexpr int kTotal = 1024 + kRingBytes + kEpiBytes + kBarBytes;
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
@@ -232,10 +237,11 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
 }
 
 template <int BN, int EPI, bool kTmaStore, bool kPair>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
-  using S = Smem<BN, kPair>;
+  constexpr int kEW = epi_warps(kTmaStore);
+  using S = Smem<BN, kPair, kEW>;
   constexpr int kStages = S::kStages;
   constexpr int kTileM = kPair ? 2 * BM : BM;
   extern __shared__ uint8_t smem_dyn[];
@@ -266,7 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_addr(&tfull[a]), 1);
       // Pair mode: the leader's accumulator is free once the epilogue warps
       // of both CTAs have drained it.
-      mbar_init(smem_addr(&tempty[a]), kPair ? 2 * kEpiWarps : kEpiWarps);
+      mbar_init(smem_addr(&tempty[a]), kPair ? 2 * kEW : kEW);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -496,12 +502,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Any row pitch (the lm_head output has an odd one): lane == row to stage
       // the accumulators in shared memory, then lane == column for coalesced
       // stores of each row segment.
-      const int ew = warp - 2;             // 0..7
+      const int ew = warp - 2;             // 0 .. kEW-1
       const int quad = warp & 3;           // TMEM lane quadrant this warp may access
-      const int half = ew >> 2;            // which half of the BN columns
+      const int half = ew >> 2;            // which part (of kEW / 4) of the BN columns
       float* stg = epi + ew * 32 * kStageRowPitch;
       constexpr int kChunks = BN / 32;
-      constexpr int kChunksPerHalf = kChunks / 2;
+      constexpr int kChunksPerHalf = kChunks / (kEW / 4);
       int acc = 0;
       uint32_t acc_phase = 0;
       for (int tile = first_tile; tile < p.num_tiles; tile += tile_step) {
@@ -610,7 +616,9 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t col
 template <int BN, int EPI, bool kTmaStore, bool kPair>
 static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm, const Params& p,
                      int grid, cudaStream_t st) {
-  using S = Smem<BN, kPair>;
+  constexpr int kEW = epi_warps(kTmaStore);
+  constexpr int kThr = (2 + kEW) * 32;
+  using S = Smem<BN, kPair, kEW>;
   static_assert(S::kTotal <= 232448, "shared memory budget exceeded");
   static_assert(S::kEpiBytes >= kEpiWarps * 4096, "TMA-store staging does not fit");
   auto kern = gemm_tc_kernel<BN, EPI, kTmaStore, kPair>;
@@ -628,9 +636,9 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
     }
   }
   if constexpr (kPair)
-    launch_pdl_cluster(kern, dim3(grid), dim3(kThreads), S::kTotal, st, 2u, ta, tb, tcm, p);
+    launch_pdl_cluster(kern, dim3(grid), dim3(kThr), S::kTotal, st, 2u, ta, tb, tcm, p);
   else
-    launch_pdl(kern, dim3(grid), dim3(kThreads), S::kTotal, st, ta, tb, tcm, p);
+    launch_pdl(kern, dim3(grid), dim3(kThr), S::kTotal, st, ta, tb, tcm, p);
   return launch_status("gemm_tc");
 }
 
