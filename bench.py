@@ -287,7 +287,7 @@ def run_ours(args, rank, world, local):
 
     def step():
         model._blocks(idx, ws)
-        model._gemm(ws.h, model.weights["lm_head.weight"], logits)
+        model._lm_head(ws, logits)
 
     for _ in range(args.warmup):
         step()

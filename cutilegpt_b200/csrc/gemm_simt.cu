@@ -142,7 +142,7 @@ extern "C" int gpt_gemm(const void* A, int64_t lda, const void* W, const void* b
     if (gpt::tc::tc_eligible(A, lda, W, K, M, N)) {
       if (M <= gpt::tc::kSkMaxM)
         return gpt::tc::gemm_skinny(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
-      return gpt::tc::gemm_bf16(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
+      return gpt::tc::gemm_bf16(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st, nullptr);
     }
     return gpt::simt::gemm<__nv_bfloat16>(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, st);
   }
@@ -157,9 +157,8 @@ extern "C" int gpt_gemm_fused(const void* A, int64_t lda, const void* W, const v
   GPT_CHECK_ARG(dtype == GPT_BF16, "gpt_gemm_fused: bf16 only");
   GPT_CHECK_ARG(epilogue >= GPT_EPI_NONE && epilogue <= GPT_EPI_BIAS_RESIDUAL, "gpt_gemm_fused: bad epilogue %d",
                 epilogue);
-  GPT_CHECK_SHAPE(M >= 0 && N >= 0 && K > 0 && M <= gpt::tc::kSkMaxM && N < (1LL << 31) && K < (1LL << 31),
-                  "gpt_gemm_fused: needs 0 <= M <= %d rows, K > 0 (M=%lld N=%lld K=%lld)", gpt::tc::kSkMaxM,
-                  (long long)M, (long long)N, (long long)K);
+  GPT_CHECK_SHAPE(M >= 0 && N >= 0 && K > 0 && M < (1LL << 31) && N < (1LL << 31) && K < (1LL << 31),
+                  "gpt_gemm_fused: bad sizes (M=%lld N=%lld K=%lld)", (long long)M, (long long)N, (long long)K);
   GPT_CHECK_SHAPE(lda >= K && ldc >= N && (epilogue != GPT_EPI_BIAS_RESIDUAL || ldr >= N),
                   "gpt_gemm_fused: leading dimension smaller than the row");
   if (M == 0 || N == 0) return GPT_OK;
@@ -178,6 +177,10 @@ extern "C" int gpt_gemm_fused(const void* A, int64_t lda, const void* W, const v
   }
   GPT_CHECK_ARG(gpt::tc::tc_eligible(A, lda, W, K, M, N),
                 "gpt_gemm_fused: operands must be 16-byte aligned with 16-byte row pitches");
-  return gpt::tc::gemm_skinny_fused(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, f, (cudaStream_t)stream);
+  if (M <= gpt::tc::kSkMaxM)
+    return gpt::tc::gemm_skinny_fused(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, f, (cudaStream_t)stream);
+  // more rows (prefill): the tcgen05 GEMM with the LayerNorm fold or row statistics
+  GPT_CHECK_ARG(!f.k_cache, "gpt_gemm_fused: the KV append is a decode extra (M <= %d)", gpt::tc::kSkMaxM);
+  return gpt::tc::gemm_bf16(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, (cudaStream_t)stream, &f);
 }
 

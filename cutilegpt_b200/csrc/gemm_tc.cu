@@ -47,7 +47,28 @@ struct Params {
   const __nv_bfloat16* resid;
   __nv_bfloat16* C;
   int64_t ldr, ldc;
+  // FUSE = 1: LayerNorm folded in (A = raw rows x, W = gamma-scaled weight):
+  //   C = rstd * (acc - mean * ln_u) + ln_v, mean / rstd from ln_stats [ln_parts][M][2]
+  // FUSE = 2: per 128-column part, (sum, sum of squares) of the stored rows -> stats_out [ceil(N/128)][M][2]
+  const float* ln_stats;
+  const float* ln_u;
+  const float* ln_v;
+  int ln_parts;
+  float ln_eps, ln_inv_k;
+  float* stats_out;
 };
+
+// mean and rstd of row `row` from the per-part (sum, sum of squares) statistics.
+__device__ __forceinline__ void ln_row_stats(const Params& p, int row, float& mean, float& rstd) {
+  float s1 = 0.f, s2 = 0.f;
+  for (int q = 0; q < p.ln_parts; ++q) {
+    const float2 v = *reinterpret_cast<const float2*>(p.ln_stats + ((int64_t)q * p.M + row) * 2);
+    s1 += v.x;
+    s2 += v.y;
+  }
+  mean = s1 * p.ln_inv_k;
+  rstd = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
+}
 
 // ---- PTX wrappers -----------------------------------------------------------
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -236,7 +257,7 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
 
-template <int BN, int EPI, bool kTmaStore, bool kPair>
+template <int BN, int EPI, bool kTmaStore, bool kPair, int FUSE = 0>
 __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const Params p) {
@@ -395,6 +416,9 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
         const int row0 = m_blk * kTileM + (int)rank * BM + quad * 32;
         const int row = row0 + lane;
         const bool row_ok = row < p.M;
+        float ln_mean = 0.f, ln_rstd = 1.f;
+        if (FUSE == 1 && row_ok) ln_row_stats(p, row, ln_mean, ln_rstd);
+        float st1 = 0.f, st2 = 0.f;   // FUSE == 2: this row's sums over the warp's columns
         // The residual row segments of every chunk of this tile are requested
         // before waiting for the accumulator, so their HBM latency overlaps
         // the tile's MMAs instead of serialising chunk after chunk.
@@ -417,9 +441,10 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
           const int c = half * kChunksPerHalf + cc;
           const int col0 = n_blk * BN + c * 32;
           const bool full = col0 + 32 <= p.N;
-          // bias and residual stay packed (bf16 pairs) until the math loop.
+          // bias and residual stay packed (bf16 pairs) until the math loop
+          // (with the LayerNorm fold the bias is part of ln_v and may be null).
           uint32_t bw[16], rw[16];
-          if (EPI != GPT_EPI_NONE) {
+          if (EPI != GPT_EPI_NONE && FUSE != 1) {
             if (full) {
               const uint4* bp = reinterpret_cast<const uint4*>(p.bias + col0);
 #pragma unroll
@@ -459,7 +484,16 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
             float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
-            if (EPI != GPT_EPI_NONE) {
+            if (FUSE == 1) {
+              // LayerNorm fold; u / v of these two columns (the same for every row: L1 hits)
+              const int cc0 = col0 + 2 * j;
+              const float2 uu = full ? __ldg(reinterpret_cast<const float2*>(p.ln_u + cc0))
+                                     : make_float2(cc0 < p.N ? p.ln_u[cc0] : 0.f, cc0 + 1 < p.N ? p.ln_u[cc0 + 1] : 0.f);
+              const float2 vv = full ? __ldg(reinterpret_cast<const float2*>(p.ln_v + cc0))
+                                     : make_float2(cc0 < p.N ? p.ln_v[cc0] : 0.f, cc0 + 1 < p.N ? p.ln_v[cc0 + 1] : 0.f);
+              v0 = ln_rstd * (v0 - ln_mean * uu.x) + vv.x;
+              v1 = ln_rstd * (v1 - ln_mean * uu.y) + vv.y;
+            } else if (EPI != GPT_EPI_NONE) {
               const float2 bf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[j]));
               v0 += bf.x; v1 += bf.y;
             }
@@ -469,6 +503,11 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
               v0 += rf.x; v1 += rf.y;
             }
             pk[j] = pack2_bf16(v0, v1);
+            if (FUSE == 2) {   // statistics of the stored (rounded) values; columns past N hold 0
+              const float2 y = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&pk[j]));
+              st1 += y.x + y.y;
+              st2 = fmaf(y.x, y.x, fmaf(y.y, y.y, st2));
+            }
           }
           // The store issued from this staging tile two chunks ago must have read it.
           if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
@@ -487,6 +526,10 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
             asm volatile("cp.async.bulk.commit_group;" ::: "memory");
           }
           sb ^= 1;
+        }
+        if (FUSE == 2 && row_ok) {   // part = 128-column half of the BN = 256 tile
+          *reinterpret_cast<float2*>(p.stats_out + ((int64_t)(n_blk * 2 + half) * p.M + row) * 2) =
+              make_float2(st1, st2);
         }
         tc_fence_before();
         __syncwarp();
@@ -516,6 +559,8 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
         if (!mbar_wait(smem_addr(&tfull[acc]), acc_phase)) break;
         tc_fence_after();
         const int row0 = m_blk * kTileM + (int)rank * BM + quad * 32;
+        float ln_mean = 0.f, ln_rstd = 1.f;   // FUSE == 1: statistics of row row0 + lane
+        if (FUSE == 1 && row0 + lane < p.M) ln_row_stats(p, row0 + lane, ln_mean, ln_rstd);
         for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
           // lane == column in the store phase below.
           const int col = n_blk * BN + c * 32 + lane;
@@ -530,8 +575,15 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
               res[rr] = (row < p.M && col_ok) ? __bfloat162float(p.resid[(int64_t)row * p.ldr + col]) : 0.f;
             }
           }
-          float bcol = 0.f;
-          if (EPI != GPT_EPI_NONE && col_ok) bcol = __bfloat162float(p.bias[col]);
+          float bcol = 0.f, ucol = 0.f;
+          if (FUSE == 1) {
+            if (col_ok) {
+              ucol = p.ln_u[col];
+              bcol = p.ln_v[col];
+            }
+          } else if (EPI != GPT_EPI_NONE && col_ok) {
+            bcol = __bfloat162float(p.bias[col]);
+          }
           uint32_t r[32];
           const uint32_t taddr = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN + c * 32);
           tmem_ld32(taddr, r);
@@ -543,8 +595,11 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
 #pragma unroll
           for (int rr = 0; rr < 32; ++rr) {
             const int row = row0 + rr;
+            const float mrr = FUSE == 1 ? __shfl_sync(0xffffffffu, ln_mean, rr) : 0.f;
+            const float rrr = FUSE == 1 ? __shfl_sync(0xffffffffu, ln_rstd, rr) : 1.f;
             if (row < p.M && col_ok) {
-              float v = stg[rr * kStageRowPitch + lane] + bcol;
+              float v = stg[rr * kStageRowPitch + lane];
+              v = FUSE == 1 ? rrr * (v - mrr * ucol) + bcol : v + bcol;
               if (EPI == GPT_EPI_BIAS_GELU) v = gelu_tanh<true>(v);
               if (EPI == GPT_EPI_BIAS_RESIDUAL) v += res[rr];
               p.C[(int64_t)row * p.ldc + col] = __float2bfloat16_rn(v);
@@ -613,7 +668,7 @@ static int make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t col
   return GPT_OK;
 }
 
-template <int BN, int EPI, bool kTmaStore, bool kPair>
+template <int BN, int EPI, bool kTmaStore, bool kPair, int FUSE = 0>
 static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tcm, const Params& p,
                      int grid, cudaStream_t st) {
   constexpr int kEW = epi_warps(kTmaStore);
@@ -621,7 +676,7 @@ static int launch_bn(const CUtensorMap& ta, const CUtensorMap& tb, const CUtenso
   using S = Smem<BN, kPair, kEW>;
   static_assert(S::kTotal <= 232448, "shared memory budget exceeded");
   static_assert(S::kEpiBytes >= kEpiWarps * 4096, "TMA-store staging does not fit");
-  auto kern = gemm_tc_kernel<BN, EPI, kTmaStore, kPair>;
+  auto kern = gemm_tc_kernel<BN, EPI, kTmaStore, kPair, FUSE>;
   // Attribute set per device the first time this instantiation runs there.
   static bool done[64] = {false};
   static std::mutex mu;
@@ -701,7 +756,10 @@ static int launch_epi(int epi, bool tma_store, const CUtensorMap& ta, const CUte
 }
 
 int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const void* R, int64_t ldr,
-              void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t st) {
+              void* C, int64_t ldc, int64_t M, int64_t N, int64_t K, int epi, cudaStream_t st,
+              const gpt_gemm_fusion* fusion) {
+  const bool f_ln = fusion && fusion->ln_stats;
+  const bool f_st = fusion && fusion->row_stats;
   int sms = device_sm_count();
   if (sms <= 0) return fail(GPT_ERR_CUDA, "no CUDA device");
   int bn = pick_bn(M, N, sms);
@@ -743,19 +801,51 @@ int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const
   p.C = (__nv_bfloat16*)C;
   p.ldr = ldr;
   p.ldc = ldc;
+  p.ln_stats = f_ln ? fusion->ln_stats : nullptr;
+  p.ln_u = f_ln ? fusion->ln_u : nullptr;
+  p.ln_v = f_ln ? fusion->ln_v : nullptr;
+  p.ln_parts = f_ln ? (int)fusion->ln_parts : 0;
+  p.ln_eps = f_ln ? fusion->ln_eps : 0.f;
+  p.ln_inv_k = 1.0f / (float)K;
+  p.stats_out = f_st ? fusion->row_stats : nullptr;
   const int slots = pair ? pair_slots(sms) : sms;  // persistent CTAs (pairs)
   int grid = p.num_tiles < slots ? p.num_tiles : slots;
   if (pair) grid *= 2;
   // TMA-store epilogue when C (and R) rows are 16-byte aligned; otherwise LSU stores.
   const bool tma_store = aligned(C, 16) && (ldc * 2) % 16 == 0 &&
                          (epi != GPT_EPI_BIAS_RESIDUAL || (aligned(R, 16) && (ldr * 2) % 16 == 0)) &&
-                         (epi == GPT_EPI_NONE || aligned(bias, 16));
+                         (epi == GPT_EPI_NONE || f_ln || aligned(bias, 16));
   CUtensorMap tcm;
   if (tma_store) {
     s = make_map(&tcm, C, M, N, ldc, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B);
     if (s) return s;
   } else {
     tcm = ta;  // unused by the LSU-store epilogue
+  }
+  if (f_ln || f_st) {
+    // Fused prefill variants: CTA-pair tiles of 256 columns (row statistics are
+    // kept per 128-column half tile); LayerNorm fold with none / bias / GELU,
+    // row statistics with the residual epilogue (TMA-store path).
+    if (!pair || bn != 256) return fail(GPT_ERR_UNSUPPORTED, "fused tcgen05 GEMM needs 256-wide CTA-pair tiles");
+    if (f_ln && f_st) return fail(GPT_ERR_UNSUPPORTED, "LayerNorm fold and row statistics in one GEMM");
+    if (f_st) {
+      if (epi != GPT_EPI_BIAS_RESIDUAL || !tma_store)
+        return fail(GPT_ERR_UNSUPPORTED, "row statistics need the aligned bias + residual epilogue");
+      return launch_bn<256, GPT_EPI_BIAS_RESIDUAL, true, true, 2>(ta, tb, tcm, p, grid, st);
+    }
+    switch (epi) {
+      case GPT_EPI_NONE:
+        return tma_store ? launch_bn<256, GPT_EPI_NONE, true, true, 1>(ta, tb, tcm, p, grid, st)
+                         : launch_bn<256, GPT_EPI_NONE, false, true, 1>(ta, tb, tcm, p, grid, st);
+      case GPT_EPI_BIAS:
+        if (!tma_store) return fail(GPT_ERR_UNSUPPORTED, "LayerNorm fold with bias needs an aligned output");
+        return launch_bn<256, GPT_EPI_BIAS, true, true, 1>(ta, tb, tcm, p, grid, st);
+      case GPT_EPI_BIAS_GELU:
+        if (!tma_store) return fail(GPT_ERR_UNSUPPORTED, "LayerNorm fold with GELU needs an aligned output");
+        return launch_bn<256, GPT_EPI_BIAS_GELU, true, true, 1>(ta, tb, tcm, p, grid, st);
+      default:
+        return fail(GPT_ERR_UNSUPPORTED, "LayerNorm fold with a residual epilogue");
+    }
   }
   if (bn == 256) {
     if (pair) return launch_epi<256, true>(epi, tma_store, ta, tb, tcm, p, grid, st);

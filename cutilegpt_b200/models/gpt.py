@@ -40,9 +40,12 @@ from .init import init_state, weight_names
 class _Workspace:
     """Activation buffers for one (B, T) prefill shape."""
 
-    def __init__(self, cfg: GPTConfig, B: int, T: int, dtype, device):
+    def __init__(self, cfg: GPTConfig, B: int, T: int, dtype, device, fold: bool = False):
         M, C = B * T, cfg.n_embd
         self.B, self.T = B, T
+        self.fold = fold
+        if fold:   # row statistics of the residual stream, two ping-pong slots [2, ceil(C/128), M, 2]
+            self.stats = torch.empty((2, (C + 127) // 128, M, 2), dtype=torch.float32, device=device)
         self.x = torch.empty((M, C), dtype=dtype, device=device)       # residual stream
         self.h = torch.empty((M, C), dtype=dtype, device=device)       # LayerNorm output
         self.qkv = torch.empty((M, 3 * C), dtype=dtype, device=device)
@@ -114,6 +117,11 @@ class CutileGPT:
         # GEMMs' epilogues) and the KV append fused into the QKV GEMM: 5 launches per block instead
         # of 9. B200, GPT-2 124M, B=64: 0.49 ms per step vs 0.54 ms for the per-op step.
         self.fold_decode = os.environ.get("GPT_DECODE_FOLD", "1") == "1"
+        # The same fold in prefill (opt-in, GPT_PREFILL_FOLD=1; bf16): 1 row-statistics launch instead
+        # of 2L + 1 LayerNorm launches. Correct and tested, but the fold epilogue costs the large
+        # prefill GEMMs more than the LayerNorm kernels it replaces (B200, M = 16384: QKV +7 us,
+        # c_fc +17 us, residual + statistics +3-5 us, lm_head +300 us vs 10.3 us per LayerNorm).
+        self.fold_prefill = os.environ.get("GPT_PREFILL_FOLD", "0") == "1"
         self._folded: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]] = None
 
     # ------------------------------------------------------------------ weights
@@ -179,6 +187,22 @@ class CutileGPT:
         t.stop()
         return out
 
+    def _gemm_fused(self, a, w, out, **kw):
+        """ops.gemm_fused under the same optional kernel timer."""
+        t = self.kernel_timer
+        if t is None:
+            return ops.gemm_fused(a, w, out, **kw)
+        t.start(2 * a.shape[0] * w.shape[0] * w.shape[1])
+        ops.gemm_fused(a, w, out, **kw)
+        t.stop()
+        return out
+
+    def _prefill_fold_ok(self, M: int) -> bool:
+        """LayerNorms folded into the prefill GEMMs: bf16, and row counts the fused GEMMs serve
+        (few-row kernel up to 128 rows, CTA-pair tcgen05 kernel above 256)."""
+        return (self.fold_prefill and self.dtype == torch.bfloat16 and self.config.n_embd % 8 == 0
+                and (M <= 128 or M > 256))
+
     # ------------------------------------------------------------------ forward
     def __call__(self, idx) -> Tuple[torch.Tensor, None]:
         return self.forward(idx)
@@ -189,12 +213,16 @@ class CutileGPT:
         if ws is None:
             if len(self._ws) >= 4:  # bounded cache of activation buffers
                 self._ws.pop(next(iter(self._ws)))
-            ws = _Workspace(self.config, B, T, self.dtype, self.device)
+            ws = _Workspace(self.config, B, T, self.dtype, self.device, fold=self._prefill_fold_ok(B * T))
             self._ws[key] = ws
+        if ws.fold:
+            self._fold_weights()
         return ws
 
     def _blocks(self, idx: torch.Tensor, ws: _Workspace, cache: Optional[torch.Tensor] = None) -> None:
-        """Embedding, all transformer blocks and ln_f; result in ws.h. Appends K/V to `cache`."""
+        """Embedding and all transformer blocks; appends K/V to `cache`. Result: ws.h = ln_f(x), or,
+        with the LayerNorm fold (ws.fold), the residual stream ws.x and its row statistics ws.last_stats
+        (ln_f is then applied by the lm_head GEMM, see _lm_head)."""
         cfg = self.config
         B, T = idx.shape
         C, H = cfg.n_embd, cfg.n_head
@@ -204,6 +232,29 @@ class CutileGPT:
         qkv4 = ws.qkv.view(B, T, 3, H, D)
         q, k, v = (qkv4[:, :, j].transpose(1, 2) for j in range(3))    # [B, H, T, D] views
         att4 = ws.att.view(B, T, H, D).transpose(1, 2)
+        if ws.fold:
+            # ln_1 / ln_2 folded into the QKV / c_fc GEMMs; the residual GEMMs emit the row
+            # statistics they need (slot 0: rows entering a block, slot 1: after its attention)
+            F = self._fold_weights()
+            eps = 1e-5
+            ops.row_stats(ws.x, ws.stats[0, :1])
+            cur = ws.stats[0, :1]
+            for i in range(cfg.n_layer):
+                p = f'h.{i}.'
+                wf, u, v_ = F[p + 'attn']
+                self._gemm_fused(ws.x, wf, ws.qkv, epilogue=L.EPI_BIAS, ln=(cur, eps, u, v_))
+                if cache is not None:
+                    ops.kv_append(ws.qkv.view(B, T, 3 * C), cache[i, 0], cache[i, 1], pos0=0)
+                ops.attention_prefill(q, k, v, att4, scale)
+                self._gemm_fused(ws.att, self._w(p + 'attn.c_proj.weight'), ws.x,
+                                 bias=self._w(p + 'attn.c_proj.bias'), resid=ws.x, row_stats=ws.stats[1])
+                wf, u, v_ = F[p + 'fc']
+                self._gemm_fused(ws.x, wf, ws.f, epilogue=L.EPI_BIAS_GELU, ln=(ws.stats[1], eps, u, v_))
+                self._gemm_fused(ws.f, self._w(p + 'mlp.c_proj.weight'), ws.x,
+                                 bias=self._w(p + 'mlp.c_proj.bias'), resid=ws.x, row_stats=ws.stats[0])
+                cur = ws.stats[0]
+            ws.last_stats = cur
+            return
         for i in range(cfg.n_layer):
             p = f'h.{i}.'
             ops.layernorm(ws.x, self._w(p + 'ln_1.weight'), self._w(p + 'ln_1.bias'), ws.h)
@@ -239,8 +290,16 @@ class CutileGPT:
             return logits, None
         ws = self._workspace(B, T)
         self._blocks(idx, ws)
-        self._gemm(ws.h, self._w('lm_head.weight'), logits.view(B * T, cfg.vocab_size))
+        self._lm_head(ws, logits.view(B * T, cfg.vocab_size))
         return logits, None
+
+    def _lm_head(self, ws: _Workspace, out: torch.Tensor) -> None:
+        """Logits of every row of the workspace: ln_f (folded into the GEMM when ws.fold) + lm_head."""
+        if ws.fold:
+            wf, u, v = self._fold_weights()['lm']
+            self._gemm_fused(ws.x, wf, out, epilogue=L.EPI_NONE, ln=(ws.last_stats, 1e-5, u, v))
+        else:
+            self._gemm(ws.h, self._w('lm_head.weight'), out)
 
     def forward_last(self, idx, out: Optional[torch.Tensor] = None,
                      cache: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -252,7 +311,12 @@ class CutileGPT:
         self._blocks(idx, ws, cache)
         if out is None:
             out = torch.empty((B, self.config.vocab_size), dtype=self.dtype, device=self.device)
-        last = ws.h.view(B, T, -1)[:, T - 1, :]          # row-strided [B, C] view
+        if ws.fold:   # ln_f on the B last rows only (into the first rows of ws.h)
+            last_x = ws.x.view(B, T, -1)[:, T - 1, :]
+            last = ws.h[:B]
+            ops.layernorm(last_x.contiguous(), self._w('ln_f.weight'), self._w('ln_f.bias'), last)
+        else:
+            last = ws.h.view(B, T, -1)[:, T - 1, :]          # row-strided [B, C] view
         self._gemm(last, self._w('lm_head.weight'), out)
         return out
 

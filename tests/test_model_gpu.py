@@ -295,3 +295,25 @@ def test_packed_weights_round_trip_on_device(tmp_path):
     a, _ = m(idx)
     b, _ = m2(idx)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,T", [(2, 512), (3, 32), (1, 200)])
+def test_prefill_layernorm_fold_matches_unfolded(B, T):
+    """Prefill with ln_1 / ln_2 / ln_f folded into the GEMMs (row statistics from the residual GEMMs)
+    against the LayerNorm-kernel path on the same weights: full logits and forward_last."""
+    cfg = GPTConfig(n_layer=3, n_head=12, n_embd=768, vocab_size=50257, block_size=1024)
+    m, _ = make(cfg, torch.bfloat16, seed=26, affine=27)
+    idx = ids(B, T, cfg.vocab_size, 28).cuda()
+    res = []
+    for fold in (True, False):
+        m.fold_prefill = fold
+        m._ws.clear()
+        assert m._workspace(B, T).fold == (fold and m._prefill_fold_ok(B * T))
+        logits, _ = m(idx)
+        res.append((logits.float(), m.forward_last(idx).float()))
+    m.fold_prefill = False
+    (a, la), (b, lb) = res
+    assert ((a - b).abs().max() / b.abs().max()).item() < 2e-2
+    assert ((la - lb).abs().max() / lb.abs().max()).item() < 2e-2
+    # forward_last applies ln_f explicitly (the folded GEMM rounds differently): equal within bf16 noise
+    assert ((la - a[:, -1]).abs().max() / a[:, -1].abs().max()).item() < 2e-2
