@@ -334,8 +334,10 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
-    if (threadIdx.x == 0) {
-      for (int d = 0; d * p.rows_per < p.Mp; ++d) {
+    {
+      // lane d of warp 0 sends owner d's row block (copies issued in parallel)
+      const int d = threadIdx.x;
+      if (d < 32 && d * p.rows_per < p.Mp) {
         const int rows = min(p.rows_per, p.Mp - d * p.rows_per);
         const uint32_t src = smem_addr(part + d * p.rows_per * 128);
         const uint32_t dst = sk_cluster_addr(smem_addr(recv + split * p.rows_per * 128), (uint32_t)d);
