@@ -561,6 +561,89 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
         const int row0 = m_blk * kTileM + (int)rank * BM + quad * 32;
         float ln_mean = 0.f, ln_rstd = 1.f;   // FUSE == 1: statistics of row row0 + lane
         if (FUSE == 1 && row0 + lane < p.M) ln_row_stats(p, row0 + lane, ln_mean, ln_rstd);
+        if constexpr (EPI == GPT_EPI_NONE) {
+          // No bias / residual (the lm_head): lane == row finishes its values and
+          // stages them as packed bf16; then each row segment is written as the
+          // 16-byte-aligned chunks it contains (8 bf16 per st.global.v4, shifted
+          // by one element when the row starts on an odd element) plus its few
+          // edge elements. A row of the odd 50257 pitch starts at element
+          // offset row mod 8 inside a 16-byte unit.
+          constexpr int kSeg = kChunksPerHalf * 32;   // columns of this warp's segment
+          constexpr int kLpr = kSeg / 8;              // lanes per row (one 16-byte chunk each)
+          constexpr int kRpi = 32 / kLpr;             // rows per store iteration
+          uint32_t* sw = reinterpret_cast<uint32_t*>(stg);   // 32 rows x 33 words
+          const int colseg = n_blk * BN + half * kSeg;
+#pragma unroll
+          for (int cc = 0; cc < kChunksPerHalf; ++cc) {
+            uint32_t r[32];
+            tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) +
+                          (uint32_t)(acc * BN + (half * kChunksPerHalf + cc) * 32), r);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
+              if (FUSE == 1) {
+                const int c0 = colseg + cc * 32 + 2 * j;
+                const float u0 = c0 < p.N ? p.ln_u[c0] : 0.f, u1 = c0 + 1 < p.N ? p.ln_u[c0 + 1] : 0.f;
+                const float w0 = c0 < p.N ? p.ln_v[c0] : 0.f, w1 = c0 + 1 < p.N ? p.ln_v[c0 + 1] : 0.f;
+                v0 = ln_rstd * (v0 - ln_mean * u0) + w0;
+                v1 = ln_rstd * (v1 - ln_mean * u1) + w1;
+              }
+              sw[lane * kStageRowPitch + cc * 16 + j] = pack2_bf16(v0, v1);
+            }
+          }
+          __syncwarp();
+          const int k8 = lane % kLpr, rsub = lane / kLpr;
+          uint16_t* C16 = reinterpret_cast<uint16_t*>(p.C);
+          const int c_mis = (int)((reinterpret_cast<uintptr_t>(p.C) >> 1) & 7);
+          if (colseg + kSeg <= p.N) {
+#pragma unroll 1
+            for (int rr0 = 0; rr0 < 32; rr0 += kRpi) {
+              const int rr = rr0 + rsub;
+              const int row = row0 + rr;
+              if (row < p.M) {
+                const int64_t g0 = (int64_t)row * p.ldc + colseg;   // element index of the segment
+                const int head = (8 - (int)((c_mis + g0) & 7)) & 7;  // elements before the first 16-byte boundary
+                const int nfull = (kSeg - head) >> 3;
+                const uint32_t* srow = sw + rr * kStageRowPitch;
+                if (k8 < nfull) {
+                  const int e0 = head + 8 * k8;
+                  const int b = e0 >> 1;
+                  uint32_t w[4];
+                  if ((e0 & 1) == 0) {
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) w[i] = srow[b + i];
+                  } else {
+                    uint32_t t[5];
+#pragma unroll
+                    for (int i = 0; i < 5; ++i) t[i] = srow[b + i];
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(t[i], t[i + 1], 16);
+                  }
+                  *reinterpret_cast<uint4*>(C16 + g0 + e0) = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                // the (head + tail) = 8 edge elements when the segment is not aligned
+                if (head != 0) {
+                  for (int i = k8; i < 8; i += kLpr) {
+                    const int e = i < head ? i : kSeg - 8 + i;
+                    C16[g0 + e] = (uint16_t)(srow[e >> 1] >> ((e & 1) * 16));
+                  }
+                }
+              }
+            }
+          } else {
+            // the segment crosses N (last vocabulary tile): element stores, lane == column
+#pragma unroll 1
+            for (int rr = 0; rr < 32; ++rr) {
+              const int row = row0 + rr;
+              if (row >= p.M) break;
+              for (int e = lane; e < kSeg; e += 32)
+                if (colseg + e < p.N)
+                  C16[(int64_t)row * p.ldc + colseg + e] =
+                      (uint16_t)(sw[rr * kStageRowPitch + (e >> 1)] >> ((e & 1) * 16));
+            }
+          }
+          __syncwarp();
+        } else
         for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
           // lane == column in the store phase below.
           const int col = n_blk * BN + c * 32 + lane;
