@@ -35,7 +35,10 @@ constexpr int kEpiWarps = 8;                       // epilogue warps, TMA-store 
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 // The LSU-store epilogue (row pitch not 16-byte aligned: the lm_head's 50257)
 // is instruction-latency-bound at two warps per scheduler: it gets 16 warps.
-constexpr int epi_warps(bool tma_store) { return tma_store ? kEpiWarps : 16; }
+#ifndef GPT_LSU_EPI_WARPS
+#define GPT_LSU_EPI_WARPS 16
+#endif
+constexpr int epi_warps(bool tma_store) { return tma_store ? kEpiWarps : GPT_LSU_EPI_WARPS; }
 constexpr int kStageRowPitch = 33;  // fp32 words per staged row (bank-conflict free)
 constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 
