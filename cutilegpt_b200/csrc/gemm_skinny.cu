@@ -6,14 +6,18 @@
 // Here the operands swap roles: a CTA multiplies a 128-row slab of W (the
 // MMA's M side) by all activation rows padded to Mp (the MMA's N side,
 // 16..256) over a slice of K. The `splits` CTAs that share one slab form a
-// thread-block cluster (split-K along the cluster): each leaves its fp32
-// partial [Mp][128] in its own shared memory, one cluster barrier later
-// every CTA reduces a slice of the rows by reading its peers' partials
-// through distributed shared memory, applies bias / GELU / residual and
-// stores C. No global workspace, no atomics, deterministic order.
+// thread-block cluster (split-K along the cluster). After its MMAs each CTA
+// stages its fp32 partial [Mp][128] in shared memory and pushes the row
+// block owned by every cluster CTA into that CTA's receive buffer with one
+// `cp.async.bulk` shared::cta -> shared::cluster copy, counted on the
+// owner's mbarrier. Each owner then sums its rows over the peers in a fixed
+// order (deterministic, no global workspace, no atomics), applies bias /
+// GELU / residual (and, in the fused variant, the LayerNorm fold, output row
+// statistics and the KV append) and stores C with 8-byte stores.
 //   warp 0 lane 0   TMA producer (W slab and A rows, 128B swizzle, ring)
 //   warp 1          TMEM allocation (Mp columns); lane 0 issues tcgen05.mma
-//   warps 0-3       epilogue: thread t owns slab row t (TMEM lane t).
+//   warps 0-3       epilogue: TMEM lane t = slab row t, then one thread per
+//                   (owner row, 4 output columns) for the reduction
 #include "common.cuh"
 
 namespace gpt {
