@@ -33,10 +33,11 @@ constexpr int BM = 128;
 constexpr int BK = 64;  // 64 bf16 = 128 bytes = one 128B-swizzle row
 constexpr int kEpiWarps = 8;                       // epilogue warps, TMA-store variants
 constexpr int kThreads = (2 + kEpiWarps) * 32;
-// The LSU-store epilogue (row pitch not 16-byte aligned: the lm_head's 50257)
-// is instruction-latency-bound at two warps per scheduler: it gets 16 warps.
+// Epilogue warps of the LSU-store variant (row pitch not 16-byte aligned: the
+// lm_head's 50257). With 16-byte chunk stores 8 warps and the deeper operand
+// ring they leave room for beat 16 warps (1146 vs 1167 us at M=16384).
 #ifndef GPT_LSU_EPI_WARPS
-#define GPT_LSU_EPI_WARPS 16
+#define GPT_LSU_EPI_WARPS 8
 #endif
 constexpr int epi_warps(bool tma_store) { return tma_store ? kEpiWarps : GPT_LSU_EPI_WARPS; }
 constexpr int kStageRowPitch = 33;  // fp32 words per staged row (bank-conflict free)
@@ -204,7 +205,7 @@ struct Smem {
   static constexpr int kABytes = BM * BK * 2;
   static constexpr int kBBytes = kBRows * BK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
-  // ring depth: what fits beside the epilogue staging (16 LSU warps stage 66 KB)
+  // ring depth: what fits beside the epilogue staging (kEW warps x 4.2 KB)
   static constexpr int kStages = kEW > kEpiWarps ? (kStageBytes <= 32768 ? 4 : 3)
                                                  : (kPair ? 6 : (BN >= 256 ? 4 : 6));
   static constexpr int kRingBytes = kStages * kStageBytes;
@@ -571,16 +572,23 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
           // by one element when the row starts on an odd element) plus its few
           // edge elements. A row of the odd 50257 pitch starts at element
           // offset row mod 8 inside a 16-byte unit.
-          constexpr int kSeg = kChunksPerHalf * 32;   // columns of this warp's segment
+          // A warp's columns go in passes of at most 64 (32 packed words per
+          // staged row, inside the 33-word pitch).
+          constexpr int kSub = kChunksPerHalf < 2 ? kChunksPerHalf : 2;   // 32-column chunks per pass
+          constexpr int kSeg = kSub * 32;             // columns of one pass
           constexpr int kLpr = kSeg / 8;              // lanes per row (one 16-byte chunk each)
           constexpr int kRpi = 32 / kLpr;             // rows per store iteration
+          static_assert(kSeg / 2 <= kStageRowPitch, "staged row exceeds the pitch");
           uint32_t* sw = reinterpret_cast<uint32_t*>(stg);   // 32 rows x 33 words
-          const int colseg = n_blk * BN + half * kSeg;
+#pragma unroll 1
+          for (int pass = 0; pass < kChunksPerHalf / kSub; ++pass) {
+          const int chunk0 = half * kChunksPerHalf + pass * kSub;
+          const int colseg = n_blk * BN + chunk0 * 32;
 #pragma unroll
-          for (int cc = 0; cc < kChunksPerHalf; ++cc) {
+          for (int cc = 0; cc < kSub; ++cc) {
             uint32_t r[32];
             tmem_ld32(tmem_base + ((uint32_t)(quad * 32) << 16) +
-                          (uint32_t)(acc * BN + (half * kChunksPerHalf + cc) * 32), r);
+                          (uint32_t)(acc * BN + (chunk0 + cc) * 32), r);
 #pragma unroll
             for (int j = 0; j < 16; ++j) {
               float v0 = __uint_as_float(r[2 * j]), v1 = __uint_as_float(r[2 * j + 1]);
@@ -646,6 +654,7 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
             }
           }
           __syncwarp();
+          }  // pass
         } else
         for (int c = half * kChunksPerHalf; c < (half + 1) * kChunksPerHalf; ++c) {
           // lane == column in the store phase below.
