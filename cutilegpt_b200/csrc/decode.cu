@@ -37,6 +37,30 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict
                                                              int64_t ld_out, int H, int64_t Tmax, int L0,
                                                              const int64_t* __restrict__ len_dev,
                                                              float scale_log2, float* __restrict__ ws) {
+  // Before the dependency wait: start pulling this CTA's cached K/V rows
+  // into L2. Rows below the current position were written by earlier steps,
+  // so the reads overlap the tail of the preceding kernel (the QKV GEMM that
+  // appends row L-1). A prefetch is only a hint: the length read here may be
+  // stale without affecting results, and is clamped to the cache.
+  {
+    int Lp = L0 + (len_dev ? (int)*reinterpret_cast<const volatile int64_t*>(len_dev) : 0);
+    Lp = max(0, min(Lp, (int)Tmax));
+    const int chunk = (Lp + gridDim.x - 1) / (int)gridDim.x;
+    const int p0 = (int)blockIdx.x * chunk, p1 = min(Lp, p0 + chunk);
+    constexpr int kPiece = 4096;   // bytes per prefetch instruction
+    const int64_t bytes = p1 > p0 ? (int64_t)(p1 - p0) * D * (int64_t)sizeof(T) : 0;
+    const int npieces = (int)((bytes + kPiece - 1) / kPiece);
+    const int64_t row0 = ((int64_t)blockIdx.y * Tmax + p0) * D;
+    for (int i = threadIdx.x; i < 2 * npieces; i += blockDim.x) {
+      const T* src = ((i & 1) ? vc : kc) + row0;
+      const int64_t off = (int64_t)(i >> 1) * kPiece;
+      const int64_t rem = bytes - off;
+      const uint32_t n = (uint32_t)(rem < kPiece ? rem : kPiece);   // whole rows: a multiple of 16 bytes
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<const char*>(src) + off),
+                   "r"(n)
+                   : "memory");
+    }
+  }
   pdl_wait();
   pdl_trigger();
   constexpr int V = 16 / sizeof(T);   // elements per lane vector

@@ -38,6 +38,7 @@ struct SkParams {
   const __nv_bfloat16* resid;
   __nv_bfloat16* C;
   int64_t ldr, ldc;
+  const __nv_bfloat16* W;  // [N][K] (row pitch K): L2 prefetch of the slice past the ring
   // Fused decode extras (gemm_skinny_kernel<EPI, true> only; each may be null):
   const float* ln_stats;  // [ln_parts][M][2] (sum, sum of squares) of A's rows: LayerNorm folded in
   const float* ln_u;      // [N] row sums of the gamma-scaled weight
@@ -220,6 +221,22 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     tc_commit(smem_addr(done));  // also covers an empty K slice (no MMA issued)
   }
   __syncwarp();
+  // The W columns of this CTA's K slice that the pre-filled ring slots do not
+  // hold are pulled into L2 before the dependency wait too (warps 2-3, two
+  // slab rows per thread; a prefetch is only a hint).
+  if (warp >= 2 && p.W) {
+    const int kc0 = (kb0 + min(kb1 - kb0, stages)) * BK, kc1 = min(kb1 * BK, p.K);
+    if (kc0 < kc1) {
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = n0 + (warp - 2) * 32 + lane + 64 * h;
+        if (row < p.N)
+          asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p.W + (int64_t)row * p.K + kc0),
+                       "r"((uint32_t)((kc1 - kc0) * 2))
+                       : "memory");
+      }
+    }
+  }
   if (!(warp == 0 && lane == 0)) pdl_wait();
 
   const int nl = warp * 32 + lane;  // row of the W slab == TMEM lane == output column
@@ -580,6 +597,7 @@ static int gemm_skinny_epi(const void* A, int64_t lda, const void* W, const SkPa
   s = make_map(&ta, A, M, K, lda, pl.Mp);
   if (s) return s;
   SkParams p = p0;
+  p.W = (const __nv_bfloat16*)W;
   p.Mp = pl.Mp;
   p.nkb = pl.nkb;
   p.kb_per = pl.kb_per;
