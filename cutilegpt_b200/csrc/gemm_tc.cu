@@ -260,6 +260,14 @@ __device__ __forceinline__ void tc_commit_pair(uint32_t bar) {
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
 }
+// Accumulator release by an epilogue warp: what the MMA issuer must not
+// overtake is this warp's TMEM reads, which tcgen05.wait::ld completed and
+// tcgen05.fence::before_thread_sync ordered. No memory needs releasing, so the
+// arrive is relaxed: a release at cluster scope would first wait for every
+// global store the warp has in flight.
+__device__ __forceinline__ void mbar_arrive_tmem_free(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
 
 template <int BN, int EPI, bool kTmaStore, bool kPair, int FUSE = 0>
 __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
@@ -538,7 +546,7 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if constexpr (kPair) mbar_arrive_cluster(tempty_leader[acc]);
+          if constexpr (kPair) mbar_arrive_tmem_free(tempty_leader[acc]);
           else mbar_arrive(tempty_leader[acc]);
         }
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
@@ -705,7 +713,7 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          if constexpr (kPair) mbar_arrive_cluster(tempty_leader[acc]);
+          if constexpr (kPair) mbar_arrive_tmem_free(tempty_leader[acc]);
           else mbar_arrive(tempty_leader[acc]);
         }
         if (++acc == 2) { acc = 0; acc_phase ^= 1; }
