@@ -341,10 +341,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // mask only where needed: the diagonal block and a block past T
         float mx = -INFINITY;
         if (diag || kbase + kSC > p.T) {
+          // keys kbase .. kbase + nvalid - 1 are inside T and not after this row
+          const int nvalid = min(p.T, diag ? row + 1 : p.T) - kbase;
 #pragma unroll
           for (int i = 0; i < kSC; ++i) {
-            const int key = kbase + i;
-            if (!(key < p.T && (!diag || key <= row))) sv[i] = -INFINITY;
+            if (i >= nvalid) sv[i] = -INFINITY;
             mx = fmaxf(mx, sv[i]);
           }
         } else {
