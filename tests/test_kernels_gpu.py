@@ -282,16 +282,18 @@ def test_argmax_and_advance(dtype):
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
 def test_argmax_edge_rows(dtype):
     V = 50257
-    x = randn(6, V, seed=41).to(dtype)
+    x = randn(7, V, seed=41).to(dtype)
     x[0, 5] = x[0, 5 + 1024] = x[0, 5 + 8 * 1024 + 3] = 50.0       # ties across threads / unroll slots
     x[1, :] = float("-inf")                                        # all -inf -> index 0
     x[2, 0] = float("nan"); x[2, 777] = 60.0; x[2, 900] = float("nan")   # NaN never wins
     x[3, V - 1] = 70.0                                             # last element
     x[4, :] = float("nan"); x[4, 12345] = -3.0                     # the only number wins
-    tok = torch.empty(6, dtype=torch.int64, device="cuda")
+    x[6, 6282] = x[6, 6283] = x[6, 40000] = 80.0                    # tie across a wide-row chunk boundary
+    tok = torch.empty(7, dtype=torch.int64, device="cuda")
     ops.argmax(x.cuda(), tok)
     assert tok.cpu().tolist()[:5] == [5, 0, 777, V - 1, 12345]
     assert tok[5].item() == x[5].float().argmax().item()
+    assert tok[6].item() == 6282
     small = randn(64, 3, seed=42).to(dtype)
     tok64 = torch.empty(64, dtype=torch.int64, device="cuda")
     ops.argmax(small.cuda(), tok64)
