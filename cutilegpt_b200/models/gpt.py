@@ -36,6 +36,10 @@ from ..kernels._common import as_cuda
 from .config import GPTConfig
 from .init import init_state, weight_names
 
+# Greedy decode steps captured into one CUDA graph (the remainder of a
+# generate call replays the one-step graph).
+_GRAPH_STEPS = 8
+
 
 class _Workspace:
     """Activation buffers for one (B, T) prefill shape."""
@@ -73,6 +77,7 @@ class _DecodeState:
         nbytes = ops.decode_workspace_bytes(B, H, D, Tmax)
         self.dec_ws = torch.empty((max(nbytes, 16),), dtype=torch.uint8, device=device)
         self.graph: Optional[torch.cuda.CUDAGraph] = None          # greedy step
+        self.graph_multi: Optional[torch.cuda.CUDAGraph] = None    # _GRAPH_STEPS greedy steps
         self.sample_graphs: Dict[Tuple[float, int], torch.cuda.CUDAGraph] = {}   # per (temperature, top_k)
         self.seed = torch.zeros((1,), dtype=torch.int64, device=device)   # RNG seed of the sampling kernel
         # fused decode step (one persistent kernel for all blocks), when the shapes allow it
@@ -488,7 +493,17 @@ class CutileGPT:
                 self._greedy_step(st, seq)
                 steps -= 1
                 self._capture(st)
-            for _ in range(steps):
+            # Several steps per graph launch: inside one graph each step's first
+            # kernel overlaps the previous step's last (programmatic dependent
+            # launch), which separate graph launches do not allow.
+            if steps >= _GRAPH_STEPS and st.graph_multi is None:
+                def multi():
+                    for _ in range(_GRAPH_STEPS):
+                        self._greedy_step(st, st.seq)
+                st.graph_multi = self._capture_fn(multi)
+            for _ in range(steps // _GRAPH_STEPS):
+                st.graph_multi.replay()
+            for _ in range(steps % _GRAPH_STEPS):
                 st.graph.replay()
         return seq.clone()
 
