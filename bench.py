@@ -11,21 +11,24 @@ no collective in the data path); value = all ranks' tokens / max-over-ranks
 device time. Inputs (weights 249 MB, logits 1.65 GB per step) exceed the
 126 MB L2, so no extra flush is done between steps.
 
-Extra keys: `decode` (batch 64 sharded across the ranks,
-128-token prompt, 128 greedy steps with the KV cache), `roofline` for the
-dominant kernel family (the tcgen05 GEMMs: CUDA events around each of their
-launches, recorded in extra instrumented steps right after the timed ones,
-because an event between two kernels holds back programmatic dependent
-launch and would slow the headline loop), `extras` (cfg 3' GELU op, cfg 2,
-cfg 1 on one GPU),
-`cpu_baseline` (the CPU oracle on the host cores), `e2e` (public API, host
-token ids in, last-position logits back to the host, every step), `clocks`.
+Extra keys: `roofline` for the dominant kernel family (the tcgen05 GEMMs:
+CUDA events around each of their launches, recorded in extra instrumented
+steps right after the timed ones, because an event between two kernels holds
+back programmatic dependent launch and would slow the headline loop) plus the
+whole-forward fraction; `e2e` (public API: host token ids in, full forward,
+last-position logits of the whole batch gathered over NCCL at N > 1 and read
+back to the host, every step); `decode` (batch 64 sharded
+across the ranks, prompt 128, 128 greedy KV-cache steps, the token gather
+inside the timed region; at N = 1 also a CPU sample with the reference's
+re-forward decode semantics); `extras` (cfg 3' GELU op, cfg 2, cfg 1 on one
+GPU; cfg 5 GPT-2 XL at every N: prefill B64 x T1024, KV-cache decode and the
+reference's windowed re-prefill decode); `cpu_baseline`; `clocks`.
 
 `--impl reference` times the reference algorithm's CPU restatement
 (oracle/ref_gpt.py, fp32, all host threads) on the same config and metric,
 each step a bounded sample (one sequence of 512 tokens); the reference
-itself (CuPy + cuTile) cannot be installed on this image, so its
-restatement stands in for it.
+itself (CuPy + cuTile) cannot run on this image, so its restatement, pinned
+to the reference's own forward/generate, stands in for it.
 """
 from __future__ import annotations
 
@@ -46,7 +49,6 @@ import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
 METRIC = "GPT-2 124M prefill tokens/s (B32xT512 per GPU, bf16)"
-METRIC_XL = "GPT-2 XL prefill tokens/s (B64xT1024 global, bf16)"
 UNIT = "tokens/s"
 
 
@@ -214,30 +216,36 @@ def run_extras(dev):
     return out
 
 
-def run_decode(args, model, cfg, rank, world, dev):
+def run_decode(model, cfg, rank, world, dev, Bg=64, P=128, S=128):
     """batch 64 sharded over the ranks, prompt 128, 128 greedy KV-cache steps.
 
-    With --model xl (config 5): batch 64, prompt 768, 256 greedy KV-cache steps. The config's own
-    1024-token prompt already fills the context, so every step would re-encode a full window (a
-    prefill per step); the shortened prompt is the named deviation that keeps 768 + 256 <= 1024.
+    Config 5 (GPT-2 XL) calls it with batch 64, prompt 768, 256 steps: the config's own 1024-token
+    prompt already fills the context, so every step would re-encode a full window (a prefill per
+    step); the shortened prompt is the named deviation that keeps 768 + 256 <= 1024.
+    The timed call is ShardedGPT.generate with gather=True: at N > 1 the NCCL all_gather of the
+    generated [B, P + S] tokens runs inside the timed region and its device time is reported.
     """
-    from cutilegpt_b200.distributed import shard_range
-    Bg, P, S = (64, 768, 256) if args.model == "xl" else (64, 128, 128)
-    lo, hi = shard_range(Bg, rank, world)
+    from cutilegpt_b200.distributed import ShardedGPT
+    sharded = ShardedGPT(model)
+    lo, hi = sharded.local_rows(Bg)
     g2 = torch.Generator().manual_seed(77)
-    prompt = torch.randint(0, cfg.vocab_size, (Bg, P), generator=g2)[lo:hi].to(dev)
-    model.generate(prompt, S, top_k=1)                 # warm-up; captures the decode-step graph
+    prompt = torch.randint(0, cfg.vocab_size, (Bg, P), generator=g2).to(dev)
+    sharded.generate(prompt, S, top_k=1)               # warm-up; captures the decode-step graph
     barrier(world)
     p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     st = model._decode_state(hi - lo, P + S)          # the state the timed generate uses
     p0.record()
-    model.forward_last(prompt, out=st.logits, cache=st.cache)   # the prefill inside generate
+    model.forward_last(prompt[lo:hi], out=st.logits, cache=st.cache)   # the prefill inside generate
     p1.record()
+    sharded.time_gather = True
+    sharded.gather_ms()
     d0.record()
-    model.generate(prompt, S, top_k=1)                 # prefill + S-1 graph-replayed decode steps
+    out = sharded.generate(prompt, S, top_k=1)         # prefill + S-1 graph-replayed steps (+ gather)
     d1.record()
     barrier(world)
+    assert out.shape == (Bg, P + S)
+    gather_ms = max_over_ranks(sharded.gather_ms(), world)
     gen_ms = max_over_ranks(d0.elapsed_time(d1), world)
     pre_ms = max_over_ranks(p0.elapsed_time(p1), world)
     dec_steps = S - 1
@@ -251,35 +259,48 @@ def run_decode(args, model, cfg, rank, world, dev):
     step_bytes = (wbytes + Bl * Lyr * 2 * C * 2 * mean_len + Bl * Lyr * 2 * C * 2
                   + Bl * cfg.vocab_size * 2)
     _, peak_gbs, src = load_peaks()
-    step_s = dec_ms / dec_steps / 1e3
-    dec = {"value": dec_tok_s, "unit": "tokens/s", "batch": Bg, "prompt": P, "steps": S,
-           "ms_per_step": dec_ms / dec_steps, "prefill_ms": pre_ms,
-           "hbm_roofline": {"achieved": step_bytes / step_s / 1e9, "peak": peak_gbs, "unit": "GB/s",
-                            "frac": step_bytes / step_s / 1e9 / peak_gbs,
-                            "bytes_per_step_per_gpu": step_bytes, "peak_source": src},
-           "scaling": "strong", "cuda_graph": True}
-    return dec
+    step_s = (dec_ms - gather_ms) / dec_steps / 1e3
+    return {"value": dec_tok_s, "unit": "tokens/s", "batch": Bg, "prompt": P, "steps": S,
+            "ms_per_step": dec_ms / dec_steps, "prefill_ms": pre_ms,
+            "gather": {"collective": "all_gather (NCCL) of the generated tokens" if world > 1 else "none (N=1)",
+                       "ms": gather_ms, "share_of_decode": gather_ms / dec_ms},
+            "hbm_roofline": {"achieved": step_bytes / step_s / 1e9, "peak": peak_gbs, "unit": "GB/s",
+                             "frac": step_bytes / step_s / 1e9 / peak_gbs,
+                             "bytes_per_step_per_gpu": step_bytes, "peak_source": src},
+            "scaling": "strong", "cuda_graph": True}
 
 
-def run_ours(args, rank, world, local):
-    from cutilegpt_b200 import CutileGPT, GPTConfig, _lib
-    from cutilegpt_b200.distributed import shard_range
+def decode_cpu_sample(model_name="gpt2", P=128, budget_s=10.0):
+    """The reference's decode semantics on the host cores: every new token re-runs the whole forward
+    over the prefix (cutile_gpt/models/gpt.py:204-206, no KV cache), greedy, one sequence of prompt P,
+    fp32 oracle with bf16-rounded weights; as many steps as fit in budget_s."""
+    from cutilegpt_b200.models.init import init_state
+    from oracle import ref_gpt as R
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    cfg = model_cfg(model_name)
+    w = R.cast_weights(init_state(cfg, 1234), dtype=torch.float32, round_to=torch.bfloat16)
+    idx = torch.randint(0, cfg.vocab_size, (1, P), generator=torch.Generator().manual_seed(77))
+    steps = 0
+    t0 = time.perf_counter()
+    with torch.no_grad():
+        while time.perf_counter() - t0 < budget_s:
+            idx = R.generate_greedy(w, cfg.n_layer, cfg.n_head, cfg.block_size, idx, 1)
+            steps += 1
+    dt = time.perf_counter() - t0
+    return {"value": steps / dt, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"1 sequence, prompt {P}, {steps} greedy steps, each a full re-forward of the prefix "
+                      f"(reference semantics, no KV cache), fp32 oracle with bf16-rounded weights"}
 
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    cfg = model_cfg(args.model)
-    if args.model == "xl":                             # config 5: global batch 64, sharded (strong scaling)
-        lo, hi = shard_range(args.batch, rank, world)
-        B = hi - lo
-    else:                                              # config 3: 32 sequences per GPU (weak scaling)
-        B = args.batch
-    T = args.seq
-    model = CutileGPT(cfg, dtype=torch.bfloat16, device=dev, seed=1234)   # same weights on every rank
-    if args.decode_only:
-        return {"dec": run_decode(args, model, cfg, rank, world, dev)}
+
+def prefill_bench(model, cfg, B, T, steps, warmup, world, rank, sample_clocks=None):
+    """Timed prefill forwards (logits at every position) of B local sequences of T tokens, then a
+    separate instrumented pass with CUDA events around every GEMM launch (events between kernels
+    hold back programmatic dependent launch, so they stay out of the timed loop)."""
+    from cutilegpt_b200 import _lib
+    dev = model.device
     gen = torch.Generator(device="cpu").manual_seed(1000 + rank)
-    idx_host = torch.randint(0, cfg.vocab_size, (B, T), generator=gen).pin_memory()
-    idx = idx_host.to(dev)
+    idx = torch.randint(0, cfg.vocab_size, (B, T), generator=gen).to(dev)
     logits = torch.empty((B * T, cfg.vocab_size), dtype=torch.bfloat16, device=dev)
     ws = model._workspace(B, T)
     timer = GemmTimer()
@@ -289,28 +310,22 @@ def run_ours(args, rank, world, local):
         model._blocks(idx, ws)
         model._lm_head(ws, logits)
 
-    for _ in range(args.warmup):
+    for _ in range(warmup):
         step()
     barrier(world)
-    clocks = ClockSampler(local)
-    clocks.start()
+    if sample_clocks is not None:
+        sample_clocks.start()
     launches0 = _lib.lib().gpt_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         step()
     e1.record()
     barrier(world)
     launches = _lib.lib().gpt_launch_count() - launches0
-    ms = e0.elapsed_time(e1)
-    clk = clocks.stop()
-    ms_max = max_over_ranks(ms, world)
-    tokens = (args.batch if args.model == "xl" else B * world) * T * args.steps
-    value = tokens / (ms_max / 1e3)
-    # Roofline of the GEMM family: a separate pass with CUDA events around every GEMM launch
-    # (events between kernels hold back programmatic dependent launch, so they stay out of the
-    # headline loop above); share = GEMM time / step time of this instrumented pass.
-    rsteps = max(3, min(args.steps, 10))
+    clk = sample_clocks.stop() if sample_clocks is not None else None
+    ms_max = max_over_ranks(e0.elapsed_time(e1), world)
+    rsteps = max(3, min(steps, 10))
     timer.enabled = True
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     r0.record()
@@ -319,24 +334,99 @@ def run_ours(args, rank, world, local):
     r1.record()
     torch.cuda.synchronize()
     timer.enabled = False
-    gemm_ms = timer.total_ms()
-    gemm_launches = len(timer.pairs)
-    gemm_flops = timer.flops
-    gemm_step_ms = r0.elapsed_time(r1)
     model.kernel_timer = None
+    out = dict(ms=ms_max / steps, launches=launches, clk=clk, gemm_ms=timer.total_ms(),
+               gemm_launches=len(timer.pairs), gemm_flops=timer.flops, gemm_steps=rsteps,
+               gemm_step_ms=r0.elapsed_time(r1))
+    del logits
+    torch.cuda.empty_cache()
+    return out
 
-    # ---- e2e: public API, host ids in (pinned), last-position logits back to the host
-    out_host = torch.empty((B, cfg.vocab_size), dtype=torch.bfloat16).pin_memory()
+
+def run_xl(args, rank, world, dev):
+    """BASELINE config 5 on every N: GPT-2 XL architecture, bf16, global batch 64 sharded over the
+    ranks (strong scaling): prefill B64 x T1024 (3 timed steps), KV-cache decode (prompt 768, 256
+    greedy steps, the named deviation) and the reference's own decode semantics past the context
+    (cutile_gpt/models/gpt.py:205: the last 1024 tokens re-encoded every step, 2 timed steps)."""
+    from cutilegpt_b200 import CutileGPT
+    from cutilegpt_b200.distributed import shard_range
+    from cutilegpt_b200.models.init import init_state
+    cfg = model_cfg("xl")
+    model = CutileGPT.__new__(CutileGPT)
+    model._setup(cfg, torch.bfloat16, dev)
+    model.load_state(init_state(cfg, 1234, device=dev))    # seeded on the device (fast); same on every rank
+    Bg, T = 64, 1024
+    lo, hi = shard_range(Bg, rank, world)
+    r = prefill_bench(model, cfg, hi - lo, T, steps=3, warmup=3, world=world, rank=rank)
+    peak_tf, _, src = load_peaks()
+    value = Bg * T / (r["ms"] / 1e3)
+    gemm_tf = r["gemm_flops"] / (r["gemm_ms"] / 1e3) / 1e12
+    model_tf = flops_per_token(cfg, T) * value / world / 1e12
+    out = {"config": "cfg5 gpt2-xl (48/25/1600) bf16, global batch 64 sharded over the ranks",
+           "prefill": {"value": value, "unit": UNIT, "batch": Bg, "seq_len": T, "ms_per_step": r["ms"],
+                       "steps": 3, "warmup": 3, "scaling": "strong",
+                       "whole_forward_tflops_per_gpu": model_tf, "whole_forward_frac": model_tf / peak_tf,
+                       "gemm_family_tflops": gemm_tf, "gemm_family_frac": gemm_tf / peak_tf,
+                       "peak_source": src}}
+    out["decode_kv_cache"] = run_decode(model, cfg, rank, world, dev, Bg=64, P=768, S=256)
+    # reference semantics: prompt 1024 fills the context; each new token re-encodes the last 1024
+    g = torch.Generator().manual_seed(78)
+    full = torch.randint(0, cfg.vocab_size, (Bg, T), generator=g)[lo:hi].to(dev)
+    model.generate(full, 1, top_k=1)                   # warm-up (windowed path)
+    barrier(world)
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record()
+    seq = model.generate(full, 2, top_k=1)             # 2 steps past the context, re-encoding windows
+    w1.record()
+    barrier(world)
+    assert seq.shape == (hi - lo, T + 2)
+    wms = max_over_ranks(w0.elapsed_time(w1), world)
+    out["decode_reference_semantics"] = {"value": Bg * 2 / (wms / 1e3), "unit": "tokens/s",
+                                         "ms_per_step": wms / 2, "steps": 2, "window": T,
+                                         "note": "no KV cache: every step is a 1024-token prefill of the "
+                                                 "cropped window, as the reference does past block_size"}
+    del model
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args, rank, world, local):
+    from cutilegpt_b200 import CutileGPT
+    from cutilegpt_b200.distributed import ShardedGPT
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = model_cfg("gpt2")
+    B, T = args.batch, args.seq                        # config 3: 32 sequences per GPU (weak scaling)
+    model = CutileGPT(cfg, dtype=torch.bfloat16, device=dev, seed=1234)   # same weights on every rank
+    if args.decode_only:
+        return {"dec": run_decode(model, cfg, rank, world, dev)}
+    clocks = ClockSampler(local)
+    r = prefill_bench(model, cfg, B, T, args.steps, args.warmup, world, rank, sample_clocks=clocks)
+    tokens = B * world * T * args.steps
+    value = tokens / (r["ms"] * args.steps / 1e3)
+
+    # ---- e2e through the public API: host token ids of the whole batch (pinned); each rank copies its
+    # rows in, runs the full forward (logits at every position), the last-position logits of the whole
+    # batch are gathered (NCCL all_gather at N > 1) and read back to the host, every step.
+    Bg = B * world
+    gen = torch.Generator(device="cpu").manual_seed(2000)
+    idx_host = torch.randint(0, cfg.vocab_size, (Bg, T), generator=gen).pin_memory()
+    out_host = torch.empty((Bg, cfg.vocab_size), dtype=torch.bfloat16).pin_memory()
+    sharded = ShardedGPT(model)
+    lo, hi = sharded.local_rows(Bg)
 
     def e2e_step():
-        d_idx = idx_host.to(dev, non_blocking=True)
-        lg, _ = model(d_idx)
-        out_host.copy_(lg[:, -1, :], non_blocking=True)
+        d_idx = torch.empty((Bg, T), dtype=torch.int64, device=dev)
+        d_idx[lo:hi].copy_(idx_host[lo:hi], non_blocking=True)   # only this rank's rows cross PCIe
+        _, last = sharded.forward_gather_last(d_idx)
+        out_host.copy_(last, non_blocking=True)
 
-    del logits
     for _ in range(args.warmup):
         e2e_step()
     barrier(world)
+    sharded.time_gather = True
+    sharded.gather_ms()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record()
     for _ in range(args.steps):
@@ -344,14 +434,21 @@ def run_ours(args, rank, world, local):
     f1.record()
     barrier(world)
     e2e_ms = max_over_ranks(f0.elapsed_time(f1), world)
+    e2e_gather = max_over_ranks(sharded.gather_ms(), world)
     e2e_value = tokens / (e2e_ms / 1e3)
     torch.cuda.empty_cache()
-    dec = None if args.no_decode else run_decode(args, model, cfg, rank, world, dev)
-    extras = run_extras(dev) if (world == 1 and args.model == "gpt2" and not args.no_decode) else None
-    return dict(value=value, ms=ms_max / args.steps, tokens=tokens, launches=launches, clk=clk,
-                gemm_ms=gemm_ms, gemm_launches=gemm_launches, gemm_flops=gemm_flops, gemm_steps=rsteps,
-                gemm_step_ms=gemm_step_ms, e2e_value=e2e_value,
-                e2e_h2d=B * T * 8, e2e_d2h=B * cfg.vocab_size * 2, dec=dec, cfg=cfg, extras=extras)
+    dec = None if args.no_decode else run_decode(model, cfg, rank, world, dev)
+    if dec is not None and rank == 0 and world == 1 and not args.no_cpu:
+        dec["cpu_baseline"] = decode_cpu_sample("gpt2")
+    extras = run_extras(dev) if (world == 1 and not args.no_decode) else None
+    del model
+    torch.cuda.empty_cache()
+    xl = None if args.no_xl else run_xl(args, rank, world, dev)
+    return dict(value=value, ms=r["ms"], tokens=tokens, launches=r["launches"], clk=r["clk"],
+                gemm_ms=r["gemm_ms"], gemm_launches=r["gemm_launches"], gemm_flops=r["gemm_flops"],
+                gemm_steps=r["gemm_steps"], gemm_step_ms=r["gemm_step_ms"], e2e_value=e2e_value,
+                e2e_gather_ms=e2e_gather / args.steps,
+                e2e_h2d=(hi - lo) * T * 8, e2e_d2h=Bg * cfg.vocab_size * 2, dec=dec, cfg=cfg, extras=extras, xl=xl)
 
 
 # --------------------------------------------------------------------------- CPU
@@ -386,8 +483,8 @@ def run_reference(args, rank):
         return
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    seq = 128 if args.model == "xl" else args.seq
-    fwd = _cpu_oracle(seq, args.model)
+    seq = args.seq
+    fwd = _cpu_oracle(seq)
     with torch.no_grad():
         fwd()
         t0 = time.perf_counter()
@@ -395,20 +492,26 @@ def run_reference(args, rank):
             fwd()
         dt = time.perf_counter() - t0
     value = seq * args.steps / dt
-    xl = args.model == "xl"
     sample = f"one sequence of {seq} tokens per step, fp32 oracle with bf16-rounded weights"
-    line = {"impl": "reference", "metric": METRIC_XL if xl else METRIC, "value": value, "unit": UNIT,
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "strong" if xl else "weak", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded random weights, uniform random token ids)",
-            "config": {"workload": (f"cfg5 gpt2-xl prefill (CPU sample: 1x{seq} tokens per step)" if xl else
-                                    f"cfg3 gpt2-124M prefill (CPU sample: 1x{seq} tokens per step)"),
-                       "model": "gpt2-xl" if xl else "gpt2-124M", "seq_len": seq},
+            "config": {"workload": f"cfg3 gpt2-124M prefill (CPU sample: 1x{seq} tokens per step)",
+                       "model": "gpt2-124M", "seq_len": seq},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "note": "the reference (CuPy + cuTile) cannot be installed on this image; the CPU restatement "
-                    "of its algorithm (oracle/ref_gpt.py) is timed instead"}
+            "note": "the reference (CuPy + cuTile) cannot run on this image: cupy is not installed and "
+                    "cuda.tile finds no tileiras compiler; the CPU restatement of its algorithm "
+                    "(oracle/ref_gpt.py, pinned to the reference's own forward/generate) is timed instead"}
     print(json.dumps(line), flush=True)
+
+
+# Per-launch DRAM traffic of the GEMM family in one cfg-3 step, from one ncu capture of the full-size
+# bench step (dram__bytes_read.sum + dram__bytes_write.sum over the gemm_tc_kernel launches of one
+# step, divided by their count); the command and the per-kernel table are in
+# profiles/gemm_tc_cfg3_dram.md. None until that capture exists.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = None
 
 
 def main():
@@ -417,19 +520,14 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--model", choices=["gpt2", "xl"], default="gpt2",
-                    help="gpt2: config 3/4 (default, the headline); xl: config 5 (GPT-2 XL architecture)")
-    ap.add_argument("--batch", type=int, default=None, help="default 32 per GPU (gpt2), 64 global (xl)")
-    ap.add_argument("--seq", type=int, default=None, help="default 512 (gpt2), 1024 (xl)")
+    ap.add_argument("--batch", type=int, default=32, help="sequences per GPU (config 3: 32)")
+    ap.add_argument("--seq", type=int, default=512)
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-xl", action="store_true", help="skip the config-5 (GPT-2 XL) extras")
     ap.add_argument("--decode-only", action="store_true", help="only the config-4 decode run (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    if args.batch is None:
-        args.batch = 64 if args.model == "xl" else 32
-    if args.seq is None:
-        args.seq = 1024 if args.model == "xl" else 512
 
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     if args.impl == "reference":
@@ -444,45 +542,45 @@ def main():
         if world > 1:
             dist.destroy_process_group()
         return
-    def xl_or(a, b):
-        return a if args.model == "xl" else b
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        cseq = 128 if args.model == "xl" else args.seq   # XL: a shorter sequence keeps the sample bounded
-        v, cores, n = cpu_sample(cseq, model=args.model)
+        v, cores, n = cpu_sample(args.seq)
         cpu = {"value": v, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{xl_or('GPT-2 XL', 'GPT-2 124M')} fp32 CPU oracle (bf16-rounded weights), "
-                         f"1 sequence x {cseq} tokens, median of {n} forwards"}
+               "sample": f"GPT-2 124M fp32 CPU oracle (bf16-rounded weights), "
+                         f"1 sequence x {args.seq} tokens, median of {n} forwards"}
     if rank == 0:
         peak_tf, _, src = load_peaks()
         achieved = r["gemm_flops"] / (r["gemm_ms"] / 1e3) / 1e12
+        model_tf = flops_per_token(r["cfg"], args.seq) * r["value"] / world / 1e12
         line = {
-            "metric": xl_or(METRIC_XL, METRIC), "value": r["value"], "unit": UNIT, "n_gpus": world,
+            "metric": METRIC, "value": r["value"], "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": r["ms"], "higher_is_better": True,
-            "scaling": xl_or("strong", "weak"),
-            "vs_baseline": None, "dtype": "bf16",
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded random-init weights, uniform random token ids)",
-            "config": {"workload": xl_or("cfg5 gpt2-xl prefill, logits at all positions",
-                                         "cfg3 gpt2-124M prefill, logits at all positions"),
-                       "model": xl_or("gpt2-xl", "gpt2-124M"),
-                       "global_batch": xl_or(args.batch, args.batch * world), "seq_len": args.seq,
+            "config": {"workload": "cfg3 gpt2-124M prefill, logits at all positions",
+                       "model": "gpt2-124M", "global_batch": args.batch * world, "seq_len": args.seq,
                        "parallelism": f"dp{world} (batch-sharded replicas)",
-                       "l2": xl_or("inputs larger than L2 (weights 3.1 GB, logits 6.6 GB per step); no flush",
-                                   "inputs larger than L2 (weights 249 MB, logits 1.65 GB per step); no flush")},
+                       "l2": "inputs larger than L2 (weights 249 MB, logits 1.65 GB per step); no flush"},
             "roofline": {"kernel": "gemm_tc_kernel (tcgen05 GEMM, all launches)", "bound": "tensor",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s", "frac": achieved / peak_tf,
-                         "traffic": None, "peak_source": src,
+                         "traffic": GEMM_TRAFFIC_BYTES_PER_LAUNCH, "peak_source": src,
                          "launches_per_step": r["gemm_launches"] // r["gemm_steps"],
                          "share_of_step": r["gemm_ms"] / r["gemm_step_ms"],
-                         "measured_in": f"{r['gemm_steps']} extra steps with CUDA events around every GEMM"},
-            "model_tflops": flops_per_token(r["cfg"], args.seq) * r["value"] / world / 1e12,
+                         "measured_in": f"{r['gemm_steps']} extra steps with CUDA events around every GEMM",
+                         "whole_forward": {"tflops": model_tf, "frac": model_tf / peak_tf,
+                                           "flop_per_forward": flops_per_token(r["cfg"], args.seq)
+                                           * args.batch * args.seq,
+                                           "note": "all algorithmic FLOPs of the forward / step time"}},
+            "model_tflops": model_tf,
             "e2e": {"value": r["e2e_value"], "unit": UNIT, "h2d_bytes_per_step": r["e2e_h2d"],
-                    "d2h_bytes_per_step": r["e2e_d2h"]},
+                    "d2h_bytes_per_step": r["e2e_d2h"], "gather_ms_per_step": r["e2e_gather_ms"],
+                    "path": "host ids -> ShardedGPT.forward_gather_last (full forward, last-position logits "
+                            "all-gathered over NCCL at N>1) -> host"},
             "gpu_launches": r["launches"],
             "cpu_baseline": cpu,
             "decode": r["dec"],
-            "extras": r["extras"],
+            "extras": dict(r["extras"] or {}, **({"cfg5_xl": r["xl"]} if r["xl"] else {})),
             "clocks": r["clk"],
         }
         print(json.dumps(line), flush=True)

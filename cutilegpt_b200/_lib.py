@@ -48,6 +48,8 @@ SIGNATURES = {
     "gpt_last_error_string": (ctypes.c_char_p, []),
     "gpt_device_error": (_i32, [ctypes.POINTER(ctypes.c_int)]),
     "gpt_sm_count": (_i32, []),
+    "gpt_set_wait_limit_ns": (_i32, [ctypes.c_uint64]),
+    "gpt_selftest_wait": (_i32, [_i32, _i32, _p, _p]),
     "gpt_launch_count": (_i64, []),
     "gpt_embedding": (_i32, [_p, _i64, _p, _i64, _i64, _p, _i32, _p]),
     "gpt_embedding_pos": (_i32, [_p, _i64, _i64, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _i32, _p]),
@@ -62,11 +64,6 @@ SIGNATURES = {
                                     _f32, _p, _i32, _p]),
     "gpt_attention_decode_noalloc": (_i32, [_p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _p,
                                             _f32, _i32, _p]),
-    "gpt_decode_fused_plan_bytes": (_i64, [_i64]),
-    "gpt_decode_fused_workspace_bytes": (_i64, [_i64, _i64]),
-    "gpt_decode_fused_plan": (_i32, [_p, _i64, _p, _i64, _i64]),
-    "gpt_decode_fused": (_i32, [_p, _i64, _i64, _i64, _i64, _p, _p, _p, _i64, _p, _i64, _p, _p, _p, _p, _p, _i64,
-                                _p]),
     "gpt_decode_advance": (_i32, [_p, _i64, _p, _i64, _i64, _p, _p]),
     "gpt_argmax": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
     "gpt_sample": (_i32, [_p, _i64, _i64, _i64, ctypes.c_float, _i64, _p, _p, _i64, _p, _i32, _p]),

@@ -87,20 +87,6 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-// Diagnostics build only (-DGPT_ATTN_TRACE): %globaltimer at fixed points of
-// CTA 0 (producer lane and softmax thread 0), read back with gpt_debug_attn_trace().
-#ifdef GPT_ATTN_TRACE
-__device__ unsigned long long g_at_trace[3][256][4];
-#define AT_STAMP(who, blk, i)                                                          \
-  do {                                                                                 \
-    if (blockIdx.x == 0 && (blk) < 256) g_at_trace[who][blk][i] = global_timer_ns();   \
-  } while (0)
-#else
-#define AT_STAMP(who, blk, i) \
-  do {                        \
-  } while (0)
-#endif
-
 __device__ __forceinline__ void softmax_bar() {
   asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
 }
@@ -261,7 +247,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             tc_mma(tmem + (uint32_t)((sg & 1) * 128), qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), idS, k > 0);
         }
         tc_commit(smem_addr(&s_full[sg & 1]));
-        AT_STAMP(0, sg, 0);
         if (sc.last_in_tile()) tc_commit(smem_addr(&q_empty[qslot]));   // Q slot free once these MMAs retire
         sc.next(p);
         ++sg;
@@ -270,9 +255,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       while (pc.valid) {
         if (sc.valid) issue_s();         // the next S overlaps the softmax of block pg
         if (ok && !mbar_wait(smem_addr(&p_full[pg & 1]), (uint32_t)((pg >> 1) & 1))) ok = false;
-        AT_STAMP(0, pg, 1);
         if (ok && !mbar_wait(smem_addr(&o_free[pg & 1]), (uint32_t)(((pg >> 1) & 1) ^ 1))) ok = false;
-        AT_STAMP(0, pg, 2);
         const int st = pg % kKvStages;
         if (ok) {
           tc_fence_after();
@@ -286,7 +269,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         }
         tc_commit(smem_addr(&o_full[pg & 1]));
         tc_commit(smem_addr(&kv_empty[st]));
-        AT_STAMP(0, pg, 3);
         pc.next(p);
         ++pg;
       }
@@ -324,7 +306,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       for (int j = 0; j < c.nblk; ++j, ++g) {
         if (!mbar_wait(smem_addr(&s_full[g & 1]), (uint32_t)((g >> 1) & 1))) ok = false;
         tc_fence_after();
-        if (tid == 0) AT_STAMP(1, g, 0);
         const int kbase = j * kKeys + part * kSC;
         const bool diag = (j == c.nblk - 1);
         float sv[kSC];
@@ -353,9 +334,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           for (int i = 0; i < kSC; ++i) mx = fmaxf(mx, sv[i]);
         }
         sm_red[g & 1][part][rl] = mx * p.scale_log2;   // scale > 0 commutes with max
-        if (tid == 0) AT_STAMP(1, g, 1);
         softmax_bar();
-        if (tid == 0) AT_STAMP(1, g, 2);
         mx = m_run;
 #pragma unroll
         for (int s2 = 0; s2 < kSplit; ++s2) mx = fmaxf(mx, sm_red[g & 1][s2][rl]);
@@ -384,13 +363,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(smem_addr(&p_full[g & 1]));
-        if (tid == 0) AT_STAMP(1, g, 3);
         if (j > 0) fold_o(g - 1, alpha_prev);
         alpha_prev = alpha;
       }
-      if (tid == 0) AT_STAMP(2, t / gridDim.x, 0);
       fold_o(g - 1, alpha_prev);
-      if (tid == 0) AT_STAMP(2, t / gridDim.x, 1);
       // row sum across the parts (sm_l is written again only after the next
       // tile's block barriers, which every reader passes first)
       sm_l[part][rl] = l_part;
@@ -400,7 +376,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       float lsum = 0.f;
 #pragma unroll
       for (int s2 = 0; s2 < kSplit; ++s2) lsum += sm_l[s2][rl];
-      if (tid == 0) AT_STAMP(2, t / gridDim.x, 2);
       {
         // row rl, columns [part*kOC, +kOC) -> 16-byte chunks of the 128-byte
         // row, XOR-swizzled by (row & 7) as the tensor map expects
@@ -425,7 +400,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         }
         (void)row;
       }
-      if (tid == 0) AT_STAMP(2, t / gridDim.x, 3);
     }
   }
   if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output tiles written
@@ -509,9 +483,3 @@ int launch(const void* q, const void* k, const void* v, void* out, int64_t B, in
 
 }  // namespace attn_tc
 }  // namespace gpt
-
-#ifdef GPT_ATTN_TRACE
-extern "C" GPT_API int gpt_debug_attn_trace(void* host) {
-  return (int)cudaMemcpyFromSymbol(host, gpt::attn_tc::g_at_trace, sizeof(gpt::attn_tc::g_at_trace));
-}
-#endif

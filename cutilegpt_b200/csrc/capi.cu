@@ -59,6 +59,16 @@ int device_sm_count() {
 
 extern "C" {
 
+int gpt_set_wait_limit_ns(uint64_t ns) {
+  GPT_CHECK_ARG(ns > 0, "gpt_set_wait_limit_ns: the limit must be positive");
+  unsigned long long v = (unsigned long long)ns;
+  cudaError_t e = cudaMemcpyToSymbol(gpt::g_wait_limit_ns, &v, sizeof(v));
+  if (e != cudaSuccess) return gpt::fail(GPT_ERR_CUDA, "gpt_set_wait_limit_ns: %s", cudaGetErrorString(e));
+  return GPT_OK;
+}
+
+
+
 int gpt_version(void) { return 1; }
 
 const char* gpt_last_error_string(void) { return gpt::t_last_error.c_str(); }

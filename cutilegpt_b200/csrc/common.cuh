@@ -105,6 +105,10 @@ __device__ unsigned int g_dev_error;
 __device__ __forceinline__ void record_device_error(unsigned int code) {
   atomicOr(&g_dev_error, code);
 }
+// Limit of every bounded wait (mbarrier phase waits of the tensor-core
+// kernels), in ns of %globaltimer. 4 s by default; gpt_set_wait_limit_ns()
+// changes it for the current device (tests shorten it to make a wait run out).
+__device__ unsigned long long g_wait_limit_ns = 4000000000ull;
 
 // ---- dtype traits ----------------------------------------------------------
 template <typename T> struct Tr;

@@ -33,7 +33,11 @@ static_assert(kNoAllocScratchBytes % 256 == 0, "scratch size must keep 256-byte 
 static __device__ __align__(256) float g_decode_scratch[kNoAllocScratchBytes / sizeof(float)];
 
 // Device address of g_decode_scratch on the current device, looked up once
-// per device (with that device current) and cached.
+// per device (with that device current) and cached for the life of the
+// process. The cache does not survive cudaDeviceReset() (or any other reset
+// of the device's primary context): the module is then loaded again and the
+// array may move, so a process that resets a device must not call this entry
+// point on it afterwards.
 static int scratch_address(void** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

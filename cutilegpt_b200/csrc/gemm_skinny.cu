@@ -98,24 +98,10 @@ __host__ __device__ inline int sk_smem_bytes(int Mp, int stages, int splits, int
 // variant's static arrays (row statistics, LayerNorm mean / rstd).
 constexpr int kSkSmemLimit = 232448 - 8192;
 
-#ifdef GPT_SK_TRACE
-__device__ unsigned long long g_sk_trace[1024 * 8];
-#define SK_STAMP(i)                                                                  \
-  do {                                                                               \
-    const unsigned cta = blockIdx.x + blockIdx.y * gridDim.x;                        \
-    if (threadIdx.x == 0 && cta < 1024) g_sk_trace[cta * 8 + (i)] = global_timer_ns(); \
-  } while (0)
-#else
-#define SK_STAMP(i) \
-  do {              \
-  } while (0)
-#endif
-
 template <int EPI, bool kFuse>
 __global__ void __launch_bounds__(kSkThreads, 4)
     gemm_skinny_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmA,
                        const SkParams p) {
-  SK_STAMP(0);
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
   constexpr int kWBytes = 128 * BK * 2;
@@ -185,10 +171,8 @@ __global__ void __launch_bounds__(kSkThreads, 4)
       mbar_expect_tx(fb, bytes);
       tma_load_2d(smem_addr(ringW + i * kWBytes), &tmW, fb, (kb0 + i) * BK, n0);
     }
-    SK_STAMP(1);
     pdl_wait();
     pdl_trigger();
-    SK_STAMP(2);
     for (int i = 0; i < pre; ++i)
       tma_load_2d(smem_addr(ringA + i * aBytes), &tmA, smem_addr(&full[i]), (kb0 + i) * BK, 0);
     int stage = pre % stages;
@@ -247,7 +231,6 @@ __global__ void __launch_bounds__(kSkThreads, 4)
   if (!clustered) {
     const bool ok = mbar_wait(smem_addr(done), 0);
     tc_fence_after();
-    SK_STAMP(3);
     if constexpr (kFuse) {
       // LayerNorm folded in (the host allows no other extra without split-K):
       // row statistics of all Mp rows into shared memory first.
@@ -342,7 +325,6 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     }
     const bool ok = mbar_wait(smem_addr(done), 0);
     tc_fence_after();
-    SK_STAMP(3);
     // Push: the partial goes to shared memory as [Mp][128] (lane == column,
     // conflict-free), then one bulk copy per owner CTA moves its contiguous
     // row block into slot [split] of the owner's receive buffer.
@@ -369,11 +351,9 @@ __global__ void __launch_bounds__(kSkThreads, 4)
             : "memory");
       }
     }
-    SK_STAMP(4);
     bool got = true;
     if (r_cnt > 0) {
       got = mbar_wait(smem_addr(recv_full), 0);
-      SK_STAMP(5);
     }
     got = __all_sync(0xffffffffu, got);  // warp-uniform: the row statistics use full-warp shuffles
     // Every owner has received its rows, so every bulk copy has finished
@@ -461,10 +441,8 @@ __global__ void __launch_bounds__(kSkThreads, 4)
         }
       }
     }
-    SK_STAMP(6);
     cluster_wait();
   }
-  SK_STAMP(7);
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -491,11 +469,6 @@ inline SkPlan sk_plan(int64_t M, int64_t N, int64_t K, int sms, int max_splits, 
   // shapes, CUDA-graph replay) this beats one or two per SM, since the next
   // kernel's CTAs need room to become resident while this one runs.
   int want = (2 * sms / 3 + pl.tiles - 1) / pl.tiles;
-  static const int forced = [] {
-    const char* e = getenv("GPT_SKINNY_SPLITS");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced > 0) want = forced;
   const int min_rows = (pl.Mp + max_rows_per - 1) / max_rows_per;
   if (want < min_splits) want = min_splits;
   if (want < min_rows) want = min_rows;
@@ -668,9 +641,3 @@ int gemm_skinny_fused(const void* A, int64_t lda, const void* W, const void* bia
 
 }  // namespace tc
 }  // namespace gpt
-
-#ifdef GPT_SK_TRACE
-extern "C" GPT_API int gpt_debug_sk_trace(void* host) {
-  return (int)cudaMemcpyFromSymbol(host, gpt::tc::g_sk_trace, sizeof(gpt::tc::g_sk_trace));
-}
-#endif

@@ -36,12 +36,8 @@ constexpr int kThreads = (2 + kEpiWarps) * 32;
 // Epilogue warps of the LSU-store variant (row pitch not 16-byte aligned: the
 // lm_head's 50257). With 16-byte chunk stores 8 warps and the deeper operand
 // ring they leave room for beat 16 warps (1146 vs 1167 us at M=16384).
-#ifndef GPT_LSU_EPI_WARPS
-#define GPT_LSU_EPI_WARPS 8
-#endif
-constexpr int epi_warps(bool tma_store) { return tma_store ? kEpiWarps : GPT_LSU_EPI_WARPS; }
+constexpr int epi_warps(bool tma_store) { return tma_store ? kEpiWarps : 8; }
 constexpr int kStageRowPitch = 33;  // fp32 words per staged row (bank-conflict free)
-constexpr uint64_t kWaitLimitNs = 4000000000ull;  // 4 s
 
 struct Params {
   int M, N, K;
@@ -106,7 +102,7 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitLimitNs) {
+    if (global_timer_ns() - t0 > g_wait_limit_ns) {
       record_device_error(GPT_DEVERR_TIMEOUT);
       return false;
     }
@@ -868,19 +864,9 @@ int gemm_bf16(const void* A, int64_t lda, const void* W, const void* bias, const
   int sms = device_sm_count();
   if (sms <= 0) return fail(GPT_ERR_CUDA, "no CUDA device");
   int bn = pick_bn(M, N, sms);
-  // GPT_GEMM_BN=128|256 overrides the tile width (tuning experiments).
-  static const int forced_bn = [] {
-    const char* e = getenv("GPT_GEMM_BN");
-    return e ? atoi(e) : 0;
-  }();
-  if (forced_bn == 128 || forced_bn == 256) bn = forced_bn;
   // CTA pairs (256-row tiles, cta_group::2) for BN = 256 once there are
-  // enough rows to fill them; GPT_GEMM_PAIR=0 forces single-CTA tiles.
-  static const int pair_env = [] {
-    const char* e = getenv("GPT_GEMM_PAIR");
-    return e ? atoi(e) : -1;
-  }();
-  const bool pair = bn == 256 && sms >= 2 && (pair_env < 0 ? M > BM : pair_env != 0);
+  // enough rows to fill them.
+  const bool pair = bn == 256 && sms >= 2 && M > BM;
   const int tile_m = pair ? 2 * BM : BM;
   CUtensorMap ta, tb;
   int s = make_map(&ta, A, M, K, lda, BM);
@@ -968,3 +954,37 @@ bool tc_eligible(const void* A, int64_t lda, const void* W, int64_t K, int64_t M
 
 }  // namespace tc
 }  // namespace gpt
+
+namespace gpt {
+namespace tc {
+
+// Self-test of the bounded wait: one CTA initialises an mbarrier that
+// expects `expected` arrivals, makes `arrivals` of them and waits for the
+// phase with the library's bounded wait (mbar_wait). With fewer arrivals
+// than expected the wait runs out after the current limit and records
+// GPT_DEVERR_TIMEOUT; out[0] = 1 if the phase completed, 0 if it timed out.
+__global__ void selftest_wait_kernel(int expected, int arrivals, int* out) {
+  __shared__ __align__(8) uint64_t bar;
+  const uint32_t b = smem_addr(&bar);
+  if (threadIdx.x == 0) {
+    mbar_init(b, (uint32_t)expected);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if ((int)threadIdx.x < arrivals) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(b) : "memory");
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) out[0] = mbar_wait(b, 0) ? 1 : 0;
+}
+
+}  // namespace tc
+}  // namespace gpt
+
+extern "C" int gpt_selftest_wait(int expected, int arrivals, int* out_dev, void* stream) {
+  GPT_CHECK_ARG(out_dev != nullptr, "gpt_selftest_wait: null out_dev");
+  GPT_CHECK_SHAPE(expected >= 1 && expected <= 32 && arrivals >= 0 && arrivals <= expected,
+                  "gpt_selftest_wait: needs 1 <= expected <= 32 and 0 <= arrivals <= expected");
+  gpt::tc::selftest_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(expected, arrivals, out_dev);
+  return gpt::launch_status("selftest_wait");
+}

@@ -83,6 +83,30 @@ class ShardedGPT:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        # With time_gather set (and CUDA tensors), CUDA events bracket every all_gather on the
+        # current stream; gather_ms() returns the device time of the gathers since the last reset.
+        self.time_gather = False
+        self._gather_events = []
+
+    def _gather(self, local: torch.Tensor, batch: int) -> torch.Tensor:
+        if not (self.time_gather and local.is_cuda):
+            return gather_batch(local, batch, self.group)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        out = gather_batch(local, batch, self.group)
+        e1.record()
+        self._gather_events.append((e0, e1))
+        return out
+
+    def gather_ms(self, reset: bool = True) -> float:
+        """Device time (ms) of the gathers recorded since the last reset (synchronises on them)."""
+        total = 0.0
+        for e0, e1 in self._gather_events:
+            e1.synchronize()
+            total += e0.elapsed_time(e1)
+        if reset:
+            self._gather_events = []
+        return total
 
     def local_rows(self, batch: int) -> Tuple[int, int]:
         return shard_range(batch, self.rank, self.world)
@@ -94,7 +118,7 @@ class ShardedGPT:
         out = self.model.generate(idx[lo:hi], max_new_tokens, **kw)
         if not gather or self.world == 1:
             return out
-        return gather_batch(out, B, self.group)
+        return self._gather(out, B)
 
     def forward_last(self, idx: torch.Tensor, gather: bool = True) -> torch.Tensor:
         """Last-position logits of this rank's rows (gathered to [B, V] if requested)."""
@@ -103,4 +127,13 @@ class ShardedGPT:
         logits = self.model.forward_last(idx[lo:hi])
         if not gather or self.world == 1:
             return logits
-        return gather_batch(logits, B, self.group)
+        return self._gather(logits, B)
+
+    def forward_gather_last(self, idx: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        """The full forward of this rank's rows (logits at every position, as CutileGPT.forward) and
+        the last-position logits of the whole batch gathered on every rank: ([b, T, V], [B, V])."""
+        B = idx.shape[0]
+        lo, hi = self.local_rows(B)
+        logits, _ = self.model(idx[lo:hi])
+        last = logits[:, -1, :].contiguous()
+        return logits, (last if self.world == 1 else self._gather(last, B))

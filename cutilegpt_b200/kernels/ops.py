@@ -210,37 +210,3 @@ def decode_advance(tok: torch.Tensor, pos_dev: torch.Tensor, seq: torch.Tensor |
     ld, n = (seq.stride(0), seq.shape[1]) if seq is not None else (0, 0)
     L.check(L.lib().gpt_decode_advance(_ptr(tok), B, _ptr(seq), ld, n, _ptr(pos_dev), L.stream_ptr()),
             "gpt_decode_advance")
-
-
-# ---- fused decode step ----------------------------------------------------------
-_BLOCK_KEYS = ('ln_1.weight', 'ln_1.bias', 'attn.c_attn.weight', 'attn.c_attn.bias', 'attn.c_proj.weight',
-               'attn.c_proj.bias', 'ln_2.weight', 'ln_2.bias', 'mlp.c_fc.weight', 'mlp.c_fc.bias',
-               'mlp.c_proj.weight', 'mlp.c_proj.bias')
-
-
-def decode_fused_plan(weights: dict, n_layer: int, n_embd: int, device) -> torch.Tensor:
-    """Device buffer with the weight tensor maps / pointers the fused decode kernel reads."""
-    import ctypes
-    nbytes = int(L.lib().gpt_decode_fused_plan_bytes(n_layer))
-    plan = torch.empty((nbytes,), dtype=torch.uint8, device=device)
-    ptrs = (ctypes.c_void_p * (12 * n_layer))(
-        *[weights[f'h.{i}.{k}'].data_ptr() for i in range(n_layer) for k in _BLOCK_KEYS])
-    L.check(L.lib().gpt_decode_fused_plan(plan.data_ptr(), nbytes, ptrs, n_layer, n_embd), "gpt_decode_fused_plan")
-    return plan
-
-
-def decode_fused_workspace_bytes(B: int, C: int) -> int:
-    return int(L.lib().gpt_decode_fused_workspace_bytes(B, C))
-
-
-def decode_fused(plan: torch.Tensor, n_layer: int, tok: torch.Tensor, pos_dev: torch.Tensor, wte: torch.Tensor,
-                 wpe: torch.Tensor, lnf_w: torch.Tensor, lnf_b: torch.Tensor, cache: torch.Tensor,
-                 h_out: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
-    """All blocks of one decode step (see include/gpt_b200.h); ln_f output into h_out [B, C]."""
-    B, C = h_out.shape
-    Tmax = cache.shape[-2]
-    L.check(L.lib().gpt_decode_fused(plan.data_ptr(), n_layer, C, B, Tmax, _ptr(tok), _ptr(pos_dev), _ptr(wte),
-                                     wte.shape[0], _ptr(wpe), wpe.shape[0], _ptr(lnf_w), _ptr(lnf_b), _ptr(cache),
-                                     _ptr(h_out), _ptr(workspace), workspace.numel(), L.stream_ptr()),
-            "gpt_decode_fused")
-    return h_out

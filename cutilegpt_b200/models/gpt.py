@@ -25,7 +25,6 @@ the forward path):
 from __future__ import annotations
 
 import math
-import os
 from typing import Dict, Optional, Tuple
 
 import torch
@@ -60,7 +59,7 @@ class _Workspace:
 class _DecodeState:
     """Buffers of the KV-cache generation loop for one (B, Tmax)."""
 
-    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device, fused: bool = True, fold: bool = True):
+    def __init__(self, cfg: GPTConfig, B: int, Tmax: int, dtype, device, fold: bool = True):
         C, H = cfg.n_embd, cfg.n_head
         D = C // H
         self.B, self.Tmax = B, Tmax
@@ -80,18 +79,13 @@ class _DecodeState:
         self.graph_multi: Optional[torch.cuda.CUDAGraph] = None    # _GRAPH_STEPS greedy steps
         self.sample_graphs: Dict[Tuple[float, int], torch.cuda.CUDAGraph] = {}   # per (temperature, top_k)
         self.seed = torch.zeros((1,), dtype=torch.int64, device=device)   # RNG seed of the sampling kernel
-        # fused decode step (one persistent kernel for all blocks), when the shapes allow it
-        self.fused = (fused and dtype == torch.bfloat16 and D == 64 and C % 128 == 0 and C <= 2048 and 1 <= B <= 64)
         # folded decode step: bf16, up to 128 rows (the split-K receive buffers of the fused GEMMs
         # fit shared memory up to there), 16-byte row pitches for the TMA operands
-        self.fold = (fold and not self.fused and dtype == torch.bfloat16 and 1 <= B <= 128 and C % 8 == 0
+        self.fold = (fold and dtype == torch.bfloat16 and 1 <= B <= 128 and C % 8 == 0
                      and cfg.n_layer >= 1)
         if self.fold:
             parts = (C + 127) // 128
             self.stats = torch.zeros((2 * cfg.n_layer + 1, parts, B, 2), dtype=torch.float32, device=device)
-        if self.fused:
-            self.fused_ws = torch.zeros((ops.decode_fused_workspace_bytes(B, C),), dtype=torch.uint8, device=device)
-            self.fused_plan = None   # built from the model's weights on first use
 
 
 class CutileGPT:
@@ -114,19 +108,16 @@ class CutileGPT:
         self._dec: Dict[Tuple[int, int], _DecodeState] = {}
         # Optional object with start(flops) / stop() around every GEMM launch.
         self.kernel_timer = None
-        # Single-kernel fused decode step (opt-in, GPT_DECODE_FUSED=1): correct and tested, but on
-        # B200 at B=64 it is still slower than the per-op step (0.90 vs 0.77 ms per GPT-2 124M step).
-        self.fused_decode = os.environ.get("GPT_DECODE_FUSED", "0") == "1"
-        # Folded decode step (default for bf16, up to 128 sequences; GPT_DECODE_FOLD=0 turns it off):
+        # Folded decode step (default for bf16, up to 128 sequences; set False for the per-op step):
         # ln_1 / ln_2 / ln_f folded into the following GEMMs (row statistics produced by the residual
         # GEMMs' epilogues) and the KV append fused into the QKV GEMM: 5 launches per block instead
         # of 9. B200, GPT-2 124M, B=64: 0.49 ms per step vs 0.54 ms for the per-op step.
-        self.fold_decode = os.environ.get("GPT_DECODE_FOLD", "1") == "1"
-        # The same fold in prefill (opt-in, GPT_PREFILL_FOLD=1; bf16): 1 row-statistics launch instead
+        self.fold_decode = True
+        # The same fold in prefill (opt-in; bf16): 1 row-statistics launch instead
         # of 2L + 1 LayerNorm launches. Correct and tested, but the fold epilogue costs the large
         # prefill GEMMs more than the LayerNorm kernels it replaces (B200, M = 16384: QKV +7 us,
         # c_fc +17 us, residual + statistics +3-5 us, lm_head +300 us vs 10.3 us per LayerNorm).
-        self.fold_prefill = os.environ.get("GPT_PREFILL_FOLD", "0") == "1"
+        self.fold_prefill = False
         self._folded: Optional[Dict[str, Tuple[torch.Tensor, torch.Tensor, torch.Tensor]]] = None
 
     # ------------------------------------------------------------------ weights
@@ -332,8 +323,7 @@ class CutileGPT:
         if st is None:
             if len(self._dec) >= 2:
                 self._dec.pop(next(iter(self._dec)))
-            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device, fused=self.fused_decode,
-                              fold=self.fold_decode)
+            st = _DecodeState(self.config, B, Tmax, self.dtype, self.device, fold=self.fold_decode)
             self._dec[key] = st
         if st.fold:
             self._fold_weights()   # eager, outside any graph capture
@@ -358,13 +348,6 @@ class CutileGPT:
     def _decode_step(self, st: _DecodeState) -> None:
         """One token per sequence at device position *st.pos: logits into st.logits."""
         cfg = self.config
-        if st.fused:
-            if st.fused_plan is None:
-                st.fused_plan = ops.decode_fused_plan(self.weights, cfg.n_layer, cfg.n_embd, self.device)
-            ops.decode_fused(st.fused_plan, cfg.n_layer, st.tok, st.pos, self._w('wte'), self._w('wpe'),
-                             self._w('ln_f.weight'), self._w('ln_f.bias'), st.cache, st.h, st.fused_ws)
-            self._gemm(st.h, self._w('lm_head.weight'), st.logits)
-            return
         C, H = cfg.n_embd, cfg.n_head
         scale = 1.0 / math.sqrt(C // H)
         B = st.B

@@ -56,6 +56,18 @@ GPT_API const char* gpt_last_error_string(void);
 /* Reads and clears the device-side error word that bounded waits set when
  * they give up (GPT_ERR_TIMEOUT). Synchronises the current device. */
 GPT_API int gpt_device_error(int* code_out);
+/* Limit, in ns, of every bounded device wait of the library's kernels on
+ * the current device (default 4 s). No reference counterpart: the
+ * reference's kernels have no bounded waits. Tests shorten it to make a
+ * wait run out; it is a library setting, not a GPU setting. */
+GPT_API int gpt_set_wait_limit_ns(uint64_t ns);
+/* Self-test of the bounded wait (no reference counterpart): one CTA waits
+ * on an mbarrier that expects `expected` arrivals (1..32) after making
+ * `arrivals` of them. With arrivals < expected the wait runs out after the
+ * current limit, the kernel returns, *out_dev = 0 and the next
+ * gpt_device_error() reports GPT_ERR_TIMEOUT; otherwise *out_dev = 1.
+ * out_dev is one device int. */
+GPT_API int gpt_selftest_wait(int expected, int arrivals, int* out_dev, void* stream);
 /* Number of SMs of the current device (0 if no device). */
 GPT_API int gpt_sm_count(void);
 /* Kernels this thread has launched through the library so far. */
@@ -158,7 +170,9 @@ GPT_API int gpt_attention_decode(const void* q, int64_t ld_q, const void* k_cach
  * held from library load until exit); sizes whose
  * gpt_attention_decode_workspace_size exceeds it return GPT_ERR_SHAPE. The
  * first call on a device looks up that array's device address, so make it
- * before any stream capture on that device. All calls on a device share the
+ * before any stream capture on that device; the address stays cached until
+ * the process exits, so do not call this entry point on a device after
+ * cudaDeviceReset(). All calls on a device share the
  * array: calls whose kernels may overlap on the GPU race on it. Nothing in
  * it needs clearing between calls. Allocates nothing. */
 #define GPT_NOALLOC_DECODE_SCRATCH_BYTES (256 * 1024)
@@ -167,30 +181,6 @@ GPT_API int gpt_attention_decode_noalloc(const void* q, int64_t ld_q,
                          int64_t ld_out, int64_t B, int64_t H, int64_t D,
                          int64_t Tmax, int64_t L, const int64_t* len_dev,
                          float scale, int dtype, void* stream);
-
-/* ---- fused decode step (no reference counterpart; see gpt_attention_decode)
- * All transformer blocks of one decode step for B <= 64 sequences as one
- * persistent cooperative kernel (bf16, head_dim 64, n_embd % 128 == 0):
- * embedding of tok[b] at position *pos_dev, then per block LN1 -> QKV ->
- * K/V append + attention over positions 0..*pos_dev -> c_proj + residual ->
- * LN2 -> c_fc + GELU -> c_proj + residual, then ln_f into h_out [B, n_embd]
- * (the lm_head GEMM input). `plan` holds the weight tensor maps and
- * per-block pointers (gpt_decode_fused_plan, once per set of weights);
- * `workspace` (gpt_decode_fused_workspace_bytes) must be zero-filled before
- * its first use and is left zeroed by every call. kv_cache is
- * [L, 2, B, H, Tmax, 64]. Calls sharing a workspace must not overlap. */
-GPT_API int64_t gpt_decode_fused_plan_bytes(int64_t L);
-GPT_API int64_t gpt_decode_fused_workspace_bytes(int64_t B, int64_t C);
-/* ptrs: 12 device pointers per block, in the order ln1_w, ln1_b, w_qkv,
- * b_qkv, w_proj, b_proj, ln2_w, ln2_b, w_fc, b_fc, w_proj2, b_proj2. */
-GPT_API int gpt_decode_fused_plan(void* plan, int64_t plan_bytes,
-                          const void* const* ptrs, int64_t L, int64_t C);
-GPT_API int gpt_decode_fused(const void* plan, int64_t L, int64_t C, int64_t B,
-                     int64_t Tmax, const int64_t* tok, const int64_t* pos_dev,
-                     const void* wte, int64_t vocab, const void* wpe,
-                     int64_t n_pos, const void* lnf_w, const void* lnf_b,
-                     void* kv_cache, void* h_out, void* workspace,
-                     int64_t workspace_bytes, void* stream);
 
 /* End of a decode step: seq[b, *pos_dev + 1] = tok[b] for b < B (seq row
  * stride ld_seq, skipped when seq is NULL), then *pos_dev += 1. Positions

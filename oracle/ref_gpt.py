@@ -6,15 +6,20 @@ it. Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may
 import it, and only as the checker or the timed CPU baseline; the product
 package never imports it.
 
-Where it is pinned: tests/golden/ holds outputs of transformers'
-GPT2LMHeadModel (an independent implementation of the same GPT-2 math) on
-seeded weights, produced by tests/golden/make_golden.py, and of
-torch.nn.functional's layer_norm / gelu(tanh) / scaled_dot_product_attention
-for the per-kernel cases; tests/test_oracle.py checks this restatement
-against them. The reference's own minGPT comparison (scripts/compare_mingpt.py,
-tests/test_gpt2_real.py) stores no values, only tolerances, so no golden
-vector comes from the reference itself; minGPT (third-party submodule
-external/minGPT, commit not visible in the mount) is not present.
+Where it is pinned (tests/test_oracle.py):
+  * tests/golden/reference_golden.pt — outputs of the reference's OWN code:
+    cutile_gpt/models/gpt.py forward (gpt.py:95-183), generate with top_k=1
+    (gpt.py:185-229, crop past block_size included) and load_from_mingpt,
+    with the cutile_* kernels bound to the reference's own CuPy oracles
+    (cupy_embedding / cupy_layer_norm / cupy_linear / cupy_gelu /
+    cupy_causal_attention) and cupy replaced by NumPy, run in float64 by
+    tests/golden/make_reference_golden.py; GPT-2 124M, nano and a crop case.
+    This restatement matches them to 1e-6 (logits) and exactly (greedy ids).
+  * tests/golden/golden.pt — transformers' GPT2LMHeadModel (an independent
+    implementation of the same math) and torch.nn.functional per-kernel
+    cases, from tests/golden/make_golden.py.
+minGPT itself (third-party submodule external/minGPT, commit not visible in
+the mount) is not present; the reference's tests store no values.
 
 Every function cites the reference file:line it follows.
 """

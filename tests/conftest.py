@@ -9,6 +9,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 GOLDEN = os.path.join(ROOT, "tests", "golden", "golden.pt")
+REF_GOLDEN = os.path.join(ROOT, "tests", "golden", "reference_golden.pt")
 
 
 def pytest_configure(config):
@@ -28,3 +29,9 @@ def pytest_collection_modifyitems(config, items):
 @pytest.fixture(scope="session")
 def golden():
     return torch.load(GOLDEN, weights_only=False)
+
+
+@pytest.fixture(scope="session")
+def ref_golden():
+    """Outputs of the reference's own CutileGPT.forward / generate (tests/golden/make_reference_golden.py)."""
+    return torch.load(REF_GOLDEN, weights_only=False)

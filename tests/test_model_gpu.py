@@ -188,49 +188,6 @@ def test_tile_api_mlp_and_attention_match_oracle(dtype):
     assert ((a.double().cpu() - ref).abs().max() / ref.abs().max()).item() < tol
 
 
-@pytest.mark.parametrize("B", [1, 3, 33, 64])
-def test_fused_decode_step_matches_layer_by_layer(B):
-    """The single-kernel decode step against the per-op decode step on the same cache and position."""
-    cfg = GPTConfig(n_layer=3, n_head=12, n_embd=768, vocab_size=50257, block_size=256)
-    m, _ = make(cfg, torch.bfloat16, seed=20 + B, affine=21)
-    idx = ids(B, 40, cfg.vocab_size, 22).cuda()
-    outs = []
-    for fused in (True, False):
-        m.fused_decode = fused
-        m._dec.clear()
-        st = m._decode_state(B, 64)
-        assert st.fused == fused
-        m.forward_last(idx, out=st.logits, cache=st.cache)
-        st.pos.fill_(40)
-        step_logits = []
-        for k in range(3):          # three consecutive steps: accumulators must stay clean
-            # both paths get the same tokens (their own argmax could differ at a bf16 near-tie)
-            st.tok.copy_(idx[:, k])
-            m._decode_step(st)
-            step_logits.append(st.logits.double().cpu().clone())
-            st.pos.add_(1)
-        outs.append((step_logits, st.cache[:, :, :, :, :43].double().cpu().clone()))
-    m.fused_decode = False
-    for a, b in zip(outs[0][0], outs[1][0]):
-        err = ((a - b).abs().max() / b.abs().max()).item()
-        assert err < 2e-2, err
-    cerr = ((outs[0][1] - outs[1][1]).abs().max() / outs[1][1].abs().max()).item()
-    assert cerr < 2e-2, cerr
-
-
-def test_fused_decode_generate_teacher_forced():
-    """generate() with the fused decode step (graph-replayed) against the oracle under teacher forcing."""
-    cfg = GPTConfig(n_layer=2, n_head=12, n_embd=768, vocab_size=50257, block_size=256)
-    m, w = make(cfg, torch.bfloat16, seed=40, affine=41)
-    m.fused_decode = True
-    idx = ids(3, 70, cfg.vocab_size, 42)
-    seq = m.generate(idx.cuda(), 24, top_k=1).cpu()
-    wb = R.cast_weights(w, round_to=torch.bfloat16)
-    noise = 2e-2 * R.gpt_forward(wb, cfg.n_layer, cfg.n_head, idx, last_only=True).abs().max().item()
-    bad, gap = teacher_forced_check(wb, cfg, seq, 70, noise)
-    assert not bad.any(), gap[bad]
-
-
 def test_generate_sampling_graph_reproducible():
     """Sampled generate (temperature / top-k, CUDA-graph replay of the sampling step): valid ids,
     identical under the same torch seed or generator, different under another."""

@@ -59,3 +59,29 @@ def test_greedy_crop_semantics():
     # the last step must equal argmax over a forward of the last 8 tokens only
     last = R.gpt_forward(w, 1, 2, seq[:, -9:-1], last_only=True).argmax(-1)
     assert torch.equal(last, seq[:, -1])
+
+
+def _ref_case_weights(c):
+    cfg = GPTConfig(**c["config"])
+    w = init_state(cfg, c["weight_seed"])
+    randomize_affine(w, cfg, c["affine_seed"])
+    return cfg, R.cast_weights(w)
+
+
+@pytest.mark.parametrize("name", ["nano", "crop", "gpt2_124m"])
+def test_oracle_vs_reference_code(ref_golden, name):
+    """The restatement against the reference's own forward/generate run under a NumPy cupy (float64)."""
+    c = ref_golden["cases"][name]
+    cfg, wd = _ref_case_weights(c)
+    logits = R.gpt_forward(wd, cfg.n_layer, cfg.n_head, c["idx"])
+    keep = c["logits_head"].shape[-1]
+    assert (logits[..., :keep] - c["logits_head"].double()).abs().max() < 1e-6
+    torch.testing.assert_close(logits.sum(-1), c["logits_sum"], atol=1e-8, rtol=1e-10)
+    torch.testing.assert_close((logits ** 2).sum(-1), c["logits_sqsum"], atol=1e-8, rtol=1e-10)
+    assert torch.equal(logits.argmax(-1), c["argmax"])
+    if c["logits_last"] is not None:
+        assert (logits[:, -1] - c["logits_last"].double()).abs().max() < 1e-6
+    seq, margins = R.generate_greedy(wd, cfg.n_layer, cfg.n_head, cfg.block_size, c["idx"], c["greedy_steps"],
+                                     return_margins=True)
+    assert torch.equal(seq, c["greedy"])
+    torch.testing.assert_close(margins, c["greedy_margins"], atol=1e-9, rtol=1e-7)
