@@ -507,6 +507,61 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_probe(name, local):
+    """One HBM-bound kernel alone, at a size whose inputs exceed the 126 MB L2, timed with CUDA events
+    (3 warm-up + 10 timed launches); the profiling command runs the same probe under ncu.
+      layernorm    x [262144, 768] bf16 -> y (403 MB read + 403 MB written per launch)
+      gelu         [512, 512, 768] bf16 -> same (403 MB + 403 MB per launch)
+      decode_attn  cfg 4 decode attention: B64, 12 heads, head_dim 64, 192 cached positions, the 12 layers'
+                   caches rotated so every launch reads a cache last touched 11 launches earlier
+                   (37.7 MB of K/V per launch, 600 MB in all)"""
+    from cutilegpt_b200.kernels import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _, peak_gbs, src = load_peaks()
+    g = torch.Generator(device="cpu").manual_seed(3)
+    if name == "layernorm":
+        x = torch.randn(262144, 768, generator=g).to(torch.bfloat16).to(dev)
+        w = torch.randn(768, generator=g).to(torch.bfloat16).to(dev)
+        b = torch.randn(768, generator=g).to(torch.bfloat16).to(dev)
+        y = torch.empty_like(x)
+        fns = [lambda: ops.layernorm(x, w, b, y)]
+        nbytes = 2 * x.numel() * 2
+    elif name == "gelu":
+        x = torch.randn(512, 512, 768, generator=g).to(torch.bfloat16).to(dev)
+        y = torch.empty_like(x)
+        fns = [lambda: ops.gelu(x, y)]
+        nbytes = 2 * x.numel() * 2
+    elif name == "decode_attn":
+        B, H, D, Tmax, Lq = 64, 12, 64, 256, 192
+        caches = [(torch.randn(B, H, Tmax, D, generator=g).to(torch.bfloat16).to(dev),
+                   torch.randn(B, H, Tmax, D, generator=g).to(torch.bfloat16).to(dev)) for _ in range(12)]
+        q = torch.randn(B, 3 * H * D, generator=g).to(torch.bfloat16).to(dev)
+        out = torch.empty(B, H * D, dtype=torch.bfloat16, device=dev)
+        ws = torch.empty(max(ops.decode_workspace_bytes(B, H, D, Lq), 16), dtype=torch.uint8, device=dev)
+        fns = [(lambda kc=kc, vc=vc: ops.attention_decode(q, kc, vc, out, Lq, ws)) for kc, vc in caches]
+        nbytes = 2 * B * H * Lq * D * 2 + q.numel() // 3 * 2 + out.numel() * 2
+    else:
+        raise SystemExit(f"unknown probe {name}")
+    i = 0
+    for _ in range(3):
+        fns[i % len(fns)]()
+        i += 1
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        fns[i % len(fns)]()
+        i += 1
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / n * 1e3
+    gbs = nbytes / (us / 1e6) / 1e9
+    print(json.dumps({"probe": name, "us_per_launch": us, "algorithmic_bytes": nbytes, "GB/s": gbs,
+                      "frac_hbm": gbs / peak_gbs, "peak_gbs": peak_gbs, "peak_source": src}), flush=True)
+
+
 # Per-launch DRAM traffic of the GEMM family in one cfg-3 step, from one ncu capture of the full-size
 # bench step (dram__bytes_read.sum + dram__bytes_write.sum over the gemm_tc_kernel launches of one
 # step, divided by their count); the command and the per-kernel table are in
@@ -526,10 +581,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-xl", action="store_true", help="skip the config-5 (GPT-2 XL) extras")
     ap.add_argument("--decode-only", action="store_true", help="only the config-4 decode run (profiling)")
+    ap.add_argument("--probe", choices=["layernorm", "gelu", "decode_attn"], default=None,
+                    help="time one HBM-bound kernel alone at a size larger than L2 (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.probe:
+        run_probe(args.probe, int(os.environ.get("LOCAL_RANK", "0")))
+        return
     if args.impl == "reference":
         run_reference(args, int(os.environ.get("RANK", "0")))
         return

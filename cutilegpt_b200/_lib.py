@@ -38,7 +38,7 @@ class GemmFusion(ctypes.Structure):
         ("ln_stats", _p), ("ln_parts", _i64), ("ln_eps", _f32), ("ln_u", _p), ("ln_v", _p),
         ("row_stats", _p),
         ("k_cache", _p), ("v_cache", _p), ("kv_heads", _i64), ("kv_dim", _i64), ("kv_tmax", _i64),
-        ("kv_pos0", _i64), ("kv_pos_dev", _p),
+        ("kv_pos0", _i64), ("kv_pos_dev", _p), ("ln_sums", _p), ("row_sums", _p),
     ]
 
 
@@ -70,6 +70,7 @@ SIGNATURES = {
     "gpt_gemm_fused": (_i32, [_p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i32,
                               ctypes.POINTER(GemmFusion), _i32, _p]),
     "gpt_row_stats": (_i32, [_p, _i64, _i64, _i64, _p, _i32, _p]),
+    "gpt_row_sums": (_i32, [_p, _i64, _i64, _i64, _p, _p, _i64, _i32, _p]),
     "gpt_lnfold_weights": (_i32, [_p, _p, _p, _p, _i64, _i64, _p, _p, _p, _i32, _p]),
 }
 

@@ -2,32 +2,35 @@
 // head_dim 64), the tcgen05 counterpart of causal_attention_kernel
 // (cutile_gpt/kernels/attention.py:24-116).
 //
-// Persistent: one CTA per SM walks 128-row query tiles (heaviest causal
-// spans first). Warp 9 lane 0 streams Q / K / V by TMA (3-stage K/V ring,
-// double-buffered Q: the next tile's Q is loaded while the current tile
-// runs); warp 8 lane 0 issues the MMAs into double-buffered S / P / O; warps
-// 0-7 do the softmax, query row r owned by threads r and r + 128 (TMEM lane
-// r, one half of the columns each; GPT_ATTN_SOFTMAX_WARPS=16 splits a row
-// over four threads, measured slower on B200). Per key block of 128:
-//   S = Q Kᵀ        tcgen05.mma M=128 N=128 K=64 into one of two TMEM S
-//                   buffers; S_{j+1} is issued before the softmax of S_j
-//   softmax         one tcgen05.ld pass per thread (64 scores), causal /
-//                   length mask, row max shared through shared memory,
-//                   P = 2^(S - m) (ex2.approx) packed bf16 into shared
-//                   memory in the 128B-swizzled K-major A-operand layout
-//   O_blk = P V     tcgen05.mma M=128 N=64 K=128, V read MN-major straight
-//                   from its TMA tile -> TMEM columns [256,320)
-//   O = O·α + O_blk in registers (α = 2^(m_old - m_new)).
-// Q, K, V arrive by TMA through 4-D tensor maps {D, H, T, B} built from the
-// caller's strides, so both the fused [B, T, 3C] QKV buffer and the
+// Persistent, one CTA per SM, two independent pipelines per CTA: pipeline s
+// (s = 0, 1) walks its own 128-row query tiles (heaviest causal spans
+// first), with its own TMA producer lane (warp 10 + s), MMA issuer lane
+// (warp 8 + s) and softmax warpgroup (warps 4s .. 4s+3, one thread per query
+// row = TMEM lane). The two pipelines share the tensor core, so one tile's
+// MMAs run while the other tile's softmax does its exponentials. Per key
+// block of 128:
+//   S = Q Kᵀ      tcgen05.mma M=128 N=128 K=64 -> TMEM (this pipeline's S)
+//   softmax       pass 1 reads S (4 x 32 columns) for the row max; pass 2
+//                 reads it again, P = 2^(S·scale - m) (ex2.approx), row sum,
+//                 P packed bf16 into TMEM (tcgen05.st), masked keys -> 0
+//   O += P V      tcgen05.mma with A = P from TMEM, B = V MN-major from its
+//                 TMA tile, accumulating in TMEM across the tile's blocks
+// The running max m only moves when a block's max exceeds it by more than
+// 2^8 (log2 domain): then O in TMEM and the row sum are rescaled once;
+// otherwise P uses the stale m (values stay below 2^8), and the final O / l
+// is the same softmax. TMEM per pipeline: S 128 columns, P 64, O 64 (512 in
+// all). Q, K, V arrive by TMA through 4-D tensor maps {D, H, T, B} built
+// from the caller's strides, so both the fused [B, T, 3C] QKV buffer and the
 // [B, H, T, D] layout are read in place; rows past T are zero-filled by TMA
-// and masked. K/V blocks are double-buffered by TMA.
+// and masked; the output tile leaves through a TMA store (rows past T
+// clipped). Every wait is bounded.
 #include "common.cuh"
 
 namespace gpt {
 namespace attn_tc {
 
 using tc::desc_sw128;
+using tc::mbar_arrive;
 using tc::mbar_expect_tx;
 using tc::mbar_init;
 using tc::mbar_wait;
@@ -38,22 +41,17 @@ using tc::tc_fence_before;
 using tc::tc_mma;
 using tc::tmem_ld32;
 
-constexpr int kRows = 128;   // query rows per CTA
+constexpr int kRows = 128;   // query rows per tile
 constexpr int kKeys = 128;   // keys per block
 constexpr int kD = 64;
-#ifndef GPT_ATTN_SOFTMAX_WARPS
-#define GPT_ATTN_SOFTMAX_WARPS 8
-#endif
-constexpr int kSoftmaxWarps = GPT_ATTN_SOFTMAX_WARPS;
-constexpr int kThreads = (kSoftmaxWarps + 2) * 32;  // softmax warps + MMA warp + TMA warp
-constexpr int kSplit = kSoftmaxWarps / 4;           // threads per query row (TMEM lane)
-constexpr int kSC = 128 / kSplit;                   // score columns per thread
-constexpr int kOC = 64 / kSplit;                    // output columns per thread
-constexpr int kTileBytes = kRows * kD * 2;   // 16 KB (Q, K or V tile)
-constexpr int kPBytes = kRows * kKeys * 2;   // 32 KB (two 64-key swizzled sub-tiles)
-constexpr int kKvStages = 3;
+constexpr int kPipes = 2;
+constexpr int kThreads = (4 * kPipes + 2 * kPipes) * 32;   // softmax warpgroups + MMA + TMA warps
+constexpr int kTileBytes = kRows * kD * 2;   // 16 KB (Q, K, V or output tile)
+constexpr int kKvStages = 2;
 constexpr int kQStages = 2;
-constexpr int kSmem = 1024 + kQStages * kTileBytes + kKvStages * 2 * kTileBytes + 2 * kPBytes + kTileBytes + 256;
+constexpr int kPipeBytes = kQStages * kTileBytes + kKvStages * 2 * kTileBytes + kTileBytes;   // 112 KB
+constexpr int kSmem = 1024 + kPipes * kPipeBytes + 512;
+constexpr float kRescale = 8.f;   // log2 of the largest P value allowed before O is rescaled
 
 __device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
                                             int c2, int c3) {
@@ -77,8 +75,6 @@ struct Params {
   int n_qblk;          // ceil(T / 128)
   int BH, n_tiles;     // B*H, B*H*n_qblk
   float scale_log2;
-  __nv_bfloat16* out;
-  int64_t osb, osh, ost;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -87,25 +83,37 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
-__device__ __forceinline__ void softmax_bar() {
-  asm volatile("bar.sync 1, %0;" ::"n"(kSoftmaxWarps * 32) : "memory");
-}
-
-// 32 lanes x 16 consecutive fp32 TMEM columns.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t* r) {
+// O += P V with P (bf16, M = 128 x K = 16 slice) read from TMEM.
+__device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accum) {
   asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accum));
+}
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+          taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  tmem_st16(taddr, r);
+  tmem_st16(taddr + 16, r + 16);
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Named barrier of one softmax warpgroup (ids 1, 2).
+__device__ __forceinline__ void wg_bar(int pipe) {
+  asm volatile("bar.sync %0, 128;" ::"r"(1 + pipe) : "memory");
 }
 
-// Walks one CTA's work: tiles t = blockIdx.x, +gridDim.x, ... (tile t = query
-// block n_qblk-1 - t/(B*H) of head t%(B*H), heaviest first), and within a
-// tile the causal key blocks 0..qb.
+// Walks one pipeline's work: tiles t = first, first + stride, ... (tile t =
+// query block n_qblk-1 - t/(B*H) of head t%(B*H), heaviest first), and within
+// a tile the causal key blocks 0..qb.
 struct Cursor {
-  int tile, j, nblk, qb, b, h;
+  int tile, j, nblk, qb, b, h, stride;
   bool valid;
   __device__ void set(int t, const Params& p) {
     tile = t;
@@ -121,7 +129,7 @@ struct Cursor {
   }
   __device__ bool last_in_tile() const { return j == nblk - 1; }
   __device__ void next(const Params& p) {
-    if (++j == nblk) set(tile + (int)gridDim.x, p);
+    if (++j == nblk) set(tile + stride, p);
   }
 };
 
@@ -132,41 +140,36 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                                                               const Params p) {
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
-  uint8_t* sQ = base;                            // [2][16 KB]: Q of this tile and the next
-  uint8_t* sK = sQ + kQStages * kTileBytes;      // [kKvStages][16 KB]
-  uint8_t* sV = sK + kKvStages * kTileBytes;     // [kKvStages][16 KB]
-  uint8_t* sP = sV + kKvStages * kTileBytes;     // [2][32 KB]: keys 0-63 | keys 64-127
-  uint8_t* sO = sP + 2 * kPBytes;                // [16 KB]: output tile staged for the TMA store
-  uint64_t* bars = (uint64_t*)(sO + kTileBytes);
-  uint64_t* q_full = bars;                       // 2 (TMA tx)
-  uint64_t* q_empty = bars + 2;                  // 2 (commit after a tile's last S)
-  uint64_t* kv_full = bars + 4;                  // kKvStages (TMA tx)
-  uint64_t* kv_empty = kv_full + kKvStages;      // kKvStages (commit after PV)
-  uint64_t* s_full = kv_empty + kKvStages;       // 2 (commit after S)
-  uint64_t* s_free = s_full + 2;                 // 2 (softmax warps)
-  uint64_t* p_full = s_free + 2;                 // 2 (softmax warps)
-  uint64_t* o_full = p_full + 2;                 // 2 (commit after PV)
-  uint64_t* o_free = o_full + 2;                 // 2 (softmax warps)
-  uint32_t* tmem_slot = (uint32_t*)(o_free + 2);
-  __shared__ float sm_red[2][kSplit][kRows];   // row-max exchange, by block parity
-  __shared__ float sm_l[kSplit][kRows];        // row-sum exchange at the end of a tile
-
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // role and pipeline of this warp
+  const int pipe = warp < 4 * kPipes ? warp / 4 : (warp - 4 * kPipes) % kPipes;
+  uint8_t* pb = base + pipe * kPipeBytes;
+  uint8_t* sQ = pb;                                // [2][16 KB]
+  uint8_t* sK = sQ + kQStages * kTileBytes;        // [kKvStages][16 KB]
+  uint8_t* sV = sK + kKvStages * kTileBytes;       // [kKvStages][16 KB]
+  uint8_t* sO = sV + kKvStages * kTileBytes;       // [16 KB] output staging
+  uint64_t* bars = (uint64_t*)(base + kPipes * kPipeBytes) + pipe * 24;
+  uint64_t* q_full = bars;                         // 2 (TMA tx)
+  uint64_t* q_empty = bars + 2;                    // 2 (commit after a tile's last S)
+  uint64_t* kv_full = bars + 4;                    // kKvStages (TMA tx)
+  uint64_t* kv_empty = bars + 4 + kKvStages;       // kKvStages (commit after PV)
+  uint64_t* s_full = bars + 4 + 2 * kKvStages;     // commit after S
+  uint64_t* s_free = s_full + 1;                   // softmax warps: S read
+  uint64_t* p_full = s_full + 2;                   // softmax warps: P written (and O rescaled)
+  uint64_t* o_full = s_full + 3;                   // commit after PV
+  uint64_t* o_free = s_full + 4;                   // softmax warps: final O read
+  uint32_t* tmem_slot = (uint32_t*)((uint64_t*)(base + kPipes * kPipeBytes) + kPipes * 24);
+
   if (tid == 0) {
-    for (int i = 0; i < kQStages; ++i) {
-      mbar_init(smem_addr(&q_full[i]), 1);
-      mbar_init(smem_addr(&q_empty[i]), 1);
-    }
-    for (int i = 0; i < kKvStages; ++i) {
-      mbar_init(smem_addr(&kv_full[i]), 1);
-      mbar_init(smem_addr(&kv_empty[i]), 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(smem_addr(&s_full[i]), 1);
-      mbar_init(smem_addr(&o_full[i]), 1);
-      mbar_init(smem_addr(&s_free[i]), kSoftmaxWarps);
-      mbar_init(smem_addr(&p_full[i]), kSoftmaxWarps);
-      mbar_init(smem_addr(&o_free[i]), kSoftmaxWarps);
+    for (int q = 0; q < kPipes; ++q) {
+      uint64_t* bq = (uint64_t*)(base + kPipes * kPipeBytes) + q * 24;
+      for (int i = 0; i < 4 + 2 * kKvStages; ++i) mbar_init(smem_addr(&bq[i]), 1);
+      uint64_t* sf = bq + 4 + 2 * kKvStages;
+      mbar_init(smem_addr(&sf[0]), 1);   // s_full
+      mbar_init(smem_addr(&sf[1]), 4);   // s_free
+      mbar_init(smem_addr(&sf[2]), 4);   // p_full
+      mbar_init(smem_addr(&sf[3]), 1);   // o_full
+      mbar_init(smem_addr(&sf[4]), 4);   // o_free
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -179,18 +182,20 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;              // S buffers at columns 0 / 128, O buffers at 256 / 320
+  // this pipeline's TMEM: S at +0 (128 columns), P at +128 (64), O at +192 (64)
+  const uint32_t tm = *tmem_slot + (uint32_t)(pipe * 256);
   pdl_wait();
   pdl_trigger();
   bool ok = true;
+  const int first = 2 * (int)blockIdx.x + pipe;
+  const int stride = 2 * (int)gridDim.x;
 
-  if (warp == kSoftmaxWarps + 1) {
-    // ------------------------------------------------ TMA producer (one lane)
-    // Q of a tile (two slots: the next tile's Q arrives while the current tile
-    // runs) and the K/V blocks (kKvStages-deep ring), in the MMA order.
+  if (warp >= 4 * kPipes + kPipes) {
+    // ------------------------------------------------ TMA producer (one lane per pipeline)
     if (lane == 0) {
       Cursor lc;
-      lc.set(blockIdx.x, p);
+      lc.stride = stride;
+      lc.set(first, p);
       int lg = 0, ql = 0;
       while (lc.valid && ok) {
         if (lc.j == 0) {
@@ -217,197 +222,182 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         ++lg;
       }
     }
-  } else if (warp == kSoftmaxWarps) {
-    // ------------------------------------------------ MMA issuer (one lane)
+  } else if (warp >= 4 * kPipes) {
+    // ------------------------------------------------ MMA issuer (one lane per pipeline)
     if (lane == 0) {
-      // kind::f16, D fp32, A/B bf16; S: both K-major, N=128; PV: B MN-major (bit 16), N=64.
+      // kind::f16, D fp32, A/B bf16; S: both K-major, N=128; PV: A from TMEM, B MN-major (bit 16), N=64.
       constexpr uint32_t idS = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kKeys >> 3) << 17) |
                                ((uint32_t)(kRows >> 4) << 24);
       constexpr uint32_t idO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kD >> 3) << 17) |
                                ((uint32_t)(kRows >> 4) << 24);
       Cursor sc, pc;                     // S-issue and PV-issue cursors
-      sc.set(blockIdx.x, p);
-      pc.set(blockIdx.x, p);
-      int sg = 0, pg = 0, qs = 0;        // S blocks, PV blocks, tiles whose S started
+      sc.stride = pc.stride = stride;
+      sc.set(first, p);
+      pc.set(first, p);
+      int sg = 0, pg = 0, qs = 0, tiles_pv = 0;
       auto issue_s = [&]() {
         const int st = sg % kKvStages;
         if (sc.j == 0) {
           if (ok && !mbar_wait(smem_addr(&q_full[qs & 1]), (uint32_t)((qs / kQStages) & 1))) ok = false;
           ++qs;
         }
-        const int qslot = (qs - 1) & 1;  // this tile's Q slot
+        const int qslot = (qs - 1) & 1;
         if (ok && !mbar_wait(smem_addr(&kv_full[st]), (uint32_t)((sg / kKvStages) & 1))) ok = false;
-        if (ok && !mbar_wait(smem_addr(&s_free[sg & 1]), (uint32_t)(((sg >> 1) & 1) ^ 1))) ok = false;
+        if (ok && sg > 0 && !mbar_wait(smem_addr(s_free), (uint32_t)((sg - 1) & 1))) ok = false;
         if (ok) {
           tc_fence_after();
           const uint64_t qd = desc_sw128(smem_addr(sQ + qslot * kTileBytes));
           const uint64_t kd = desc_sw128(smem_addr(sK + st * kTileBytes));
 #pragma unroll
           for (int k = 0; k < kD / 16; ++k)
-            tc_mma(tmem + (uint32_t)((sg & 1) * 128), qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), idS, k > 0);
+            tc_mma(tm, qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), idS, k > 0);
         }
-        tc_commit(smem_addr(&s_full[sg & 1]));
+        tc_commit(smem_addr(s_full));
         if (sc.last_in_tile()) tc_commit(smem_addr(&q_empty[qslot]));   // Q slot free once these MMAs retire
         sc.next(p);
         ++sg;
       };
       if (sc.valid) issue_s();
       while (pc.valid) {
-        if (sc.valid) issue_s();         // the next S overlaps the softmax of block pg
-        if (ok && !mbar_wait(smem_addr(&p_full[pg & 1]), (uint32_t)((pg >> 1) & 1))) ok = false;
-        if (ok && !mbar_wait(smem_addr(&o_free[pg & 1]), (uint32_t)(((pg >> 1) & 1) ^ 1))) ok = false;
+        if (sc.valid) issue_s();         // the next S is computed while the softmax of block pg runs
+        if (ok && !mbar_wait(smem_addr(p_full), (uint32_t)(pg & 1))) ok = false;
+        if (pc.j == 0) {                 // a new tile overwrites O: the previous tile's O must have been read
+          if (ok && tiles_pv > 0 && !mbar_wait(smem_addr(o_free), (uint32_t)((tiles_pv - 1) & 1))) ok = false;
+          ++tiles_pv;
+        }
         const int st = pg % kKvStages;
         if (ok) {
           tc_fence_after();
           const uint64_t vd = desc_sw128(smem_addr(sV + st * kTileBytes));
-          const uint32_t pbase = smem_addr(sP + (pg & 1) * kPBytes);
 #pragma unroll
-          for (int kk = 0; kk < kKeys / 16; ++kk) {
-            const uint64_t pd = desc_sw128(pbase + (uint32_t)((kk >> 2) * (kRows * 128))) + (uint64_t)(2 * (kk & 3));
-            tc_mma(tmem + 256 + (uint32_t)((pg & 1) * 64), pd, vd + (uint64_t)(kk * 128), idO, kk > 0);  // +16 keys
-          }
+          for (int kk = 0; kk < kKeys / 16; ++kk)   // 16 keys: 8 packed P columns, 16 V rows (2 KB)
+            tc_mma_ts(tm + 192, tm + 128 + (uint32_t)(kk * 8), vd + (uint64_t)(kk * 128), idO,
+                      (pc.j > 0 || kk > 0) ? 1u : 0u);
         }
-        tc_commit(smem_addr(&o_full[pg & 1]));
+        tc_commit(smem_addr(o_full));
         tc_commit(smem_addr(&kv_empty[st]));
         pc.next(p);
         ++pg;
       }
     }
   } else {
-    // ------------------------------------------------ softmax: threads r, r+128, ... share query row r
-    static_assert((kSC == 32 && kOC == 16) || (kSC == 64 && kOC == 32), "2 or 4 threads per query row");
+    // ------------------------------------------------ softmax: thread = query row = TMEM lane
     const int rl = tid & (kRows - 1);
-    const int part = tid >> 7;                       // this thread's quarter of the keys / O columns
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    int g = 0;   // global block counter (same order as the producer)
-    for (int t = blockIdx.x; t < p.n_tiles; t += gridDim.x) {
+    const uint32_t tS = tm + lane_off, tP = tm + 128 + lane_off, tO = tm + 192 + lane_off;
+    int g = 0;   // blocks of this pipeline so far
+    for (int t = first; t < p.n_tiles; t += stride) {
       Cursor c;
+      c.stride = stride;
       c.set(t, p);
       const int row = c.qb * kRows + rl;
-      float o[kOC];
-#pragma unroll
-      for (int d = 0; d < kOC; ++d) o[d] = 0.f;
-      float m_run = -INFINITY, l_part = 0.f, alpha_prev = 1.f;
-      // O_i (relative to m_i) folded into o (relative to m_{i-1}) with alpha_i.
-      auto fold_o = [&](int gi, float alpha_i) {
-        if (!mbar_wait(smem_addr(&o_full[gi & 1]), (uint32_t)((gi >> 1) & 1))) ok = false;
-        tc_fence_after();
-        uint32_t r[kOC];
-        if constexpr (kOC == 16)
-          tmem_ld16(tmem + 256 + (uint32_t)((gi & 1) * 64 + part * kOC) + lane_off, r);
-        else
-          tmem_ld32(tmem + 256 + (uint32_t)((gi & 1) * 64 + part * kOC) + lane_off, r);
-#pragma unroll
-        for (int d = 0; d < kOC; ++d) o[d] = o[d] * alpha_i + __uint_as_float(r[d]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(smem_addr(&o_free[gi & 1]));
-      };
+      float m_use = -INFINITY, l = 0.f;
       for (int j = 0; j < c.nblk; ++j, ++g) {
-        if (!mbar_wait(smem_addr(&s_full[g & 1]), (uint32_t)((g >> 1) & 1))) ok = false;
+        if (!mbar_wait(smem_addr(s_full), (uint32_t)(g & 1))) ok = false;
         tc_fence_after();
-        const int kbase = j * kKeys + part * kSC;
-        const bool diag = (j == c.nblk - 1);
-        float sv[kSC];
-#pragma unroll
-        for (int c2 = 0; c2 < kSC; c2 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tmem + (uint32_t)((g & 1) * 128 + part * kSC + c2) + lane_off, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) sv[c2 + i] = __uint_as_float(r[i]);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) tc::mbar_arrive(smem_addr(&s_free[g & 1]));   // S buffer may be overwritten
-        // mask only where needed: the diagonal block and a block past T
+        const int kbase = j * kKeys;
+        // keys kbase .. kbase + nvalid - 1 are inside T and not after this row
+        const int nvalid = min(p.T, j == c.nblk - 1 ? row + 1 : p.T) - kbase;
         float mx = -INFINITY;
-        if (diag || kbase + kSC > p.T) {
-          // keys kbase .. kbase + nvalid - 1 are inside T and not after this row
-          const int nvalid = min(p.T, diag ? row + 1 : p.T) - kbase;
 #pragma unroll
-          for (int i = 0; i < kSC; ++i) {
-            if (i >= nvalid) sv[i] = -INFINITY;
-            mx = fmaxf(mx, sv[i]);
-          }
-        } else {
+        for (int c2 = 0; c2 < kKeys; c2 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tS + (uint32_t)c2, r);
 #pragma unroll
-          for (int i = 0; i < kSC; ++i) mx = fmaxf(mx, sv[i]);
+          for (int i = 0; i < 32; ++i)
+            if (c2 + i < nvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
         }
-        sm_red[g & 1][part][rl] = mx * p.scale_log2;   // scale > 0 commutes with max
-        softmax_bar();
-        mx = m_run;
+        mx *= p.scale_log2;   // scale > 0 commutes with max
+        bool rescale = false;
+        float alpha = 1.f;
+        if (j == 0) {
+          m_use = mx;
+        } else if (mx > m_use + kRescale) {
+          alpha = ex2(m_use - mx);
+          m_use = mx;
+          rescale = true;
+        }
+        // P and O of the previous block are free once its PV has completed
+        if (g > 0 && !mbar_wait(smem_addr(o_full), (uint32_t)((g - 1) & 1))) ok = false;
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, rescale)) {   // whole warp: tcgen05.ld / st are warp-wide
+          uint32_t r[32];
 #pragma unroll
-        for (int s2 = 0; s2 < kSplit; ++s2) mx = fmaxf(mx, sm_red[g & 1][s2][rl]);
-        const float mref = mx == -INFINITY ? 0.f : mx;
-        const float alpha = ex2(m_run - mref);
+          for (int c2 = 0; c2 < kD; c2 += 32) {
+            tmem_ld32(tO + (uint32_t)c2, r);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st32(tO + (uint32_t)c2, r);
+          }
+          l *= alpha;
+        }
         float rs = 0.f;
-        // keys [part*kSC, +kSC): sub-tile (part*kSC)/64 (64 keys, 128B-swizzled
-        // K-major rows), 16-byte chunks from ((part*kSC) % 64) / 8 of row rl
-        uint8_t* prow = sP + (g & 1) * kPBytes + ((part * kSC) >> 6) * (kRows * 128) + rl * 128;
 #pragma unroll
-        for (int q = 0; q < kSC / 8; ++q) {
-          uint32_t w[4];
+        for (int c2 = 0; c2 < kKeys; c2 += 32) {
+          uint32_t r[32];
+          tmem_ld32(tS + (uint32_t)c2, r);
+          if (c2 == kKeys - 32) {        // S fully read: the next S may overwrite it
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_addr(s_free));
+          }
+          uint32_t w[16];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float p0 = ex2(fmaf(sv[8 * q + 2 * u], p.scale_log2, -mref));
-            const float p1 = ex2(fmaf(sv[8 * q + 2 * u + 1], p.scale_log2, -mref));
+          for (int i = 0; i < 16; ++i) {
+            const float p0 = c2 + 2 * i < nvalid ? ex2(fmaf(__uint_as_float(r[2 * i]), p.scale_log2, -m_use)) : 0.f;
+            const float p1 =
+                c2 + 2 * i + 1 < nvalid ? ex2(fmaf(__uint_as_float(r[2 * i + 1]), p.scale_log2, -m_use)) : 0.f;
             rs += p0 + p1;
             __nv_bfloat162 bp = __floats2bfloat162_rn(p0, p1);
-            w[u] = *reinterpret_cast<uint32_t*>(&bp);
+            w[i] = *reinterpret_cast<uint32_t*>(&bp);
           }
-          const int chunk = ((part * kSC) & 63) / 8 + q;
-          *reinterpret_cast<uint4*>(prow + ((chunk ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          tmem_st16(tP + (uint32_t)(c2 / 2), w);
         }
-        l_part = l_part * alpha + rs;
-        m_run = mx;
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // P visible to the MMA
+        l += rs;
+        tmem_wait_st();
+        tc_fence_before();
         __syncwarp();
-        if (lane == 0) tc::mbar_arrive(smem_addr(&p_full[g & 1]));
-        if (j > 0) fold_o(g - 1, alpha_prev);
-        alpha_prev = alpha;
+        if (lane == 0) mbar_arrive(smem_addr(p_full));
       }
-      fold_o(g - 1, alpha_prev);
-      // row sum across the parts (sm_l is written again only after the next
-      // tile's block barriers, which every reader passes first)
-      sm_l[part][rl] = l_part;
+      // final O of the tile: after its last PV
+      if (!mbar_wait(smem_addr(o_full), (uint32_t)((g - 1) & 1))) ok = false;
+      tc_fence_after();
+      uint32_t o[kD];
+      tmem_ld32(tO, o);
+      tmem_ld32(tO + 32, o + 32);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(o_free));
       // the previous tile's TMA store has finished reading sO before it is rewritten
-      if (tid == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-      softmax_bar();
-      float lsum = 0.f;
+      if (rl == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      wg_bar(pipe);
+      const float inv = __fdividef(1.f, l);
+      uint8_t* srow = sO + rl * 128;
 #pragma unroll
-      for (int s2 = 0; s2 < kSplit; ++s2) lsum += sm_l[s2][rl];
-      {
-        // row rl, columns [part*kOC, +kOC) -> 16-byte chunks of the 128-byte
-        // row, XOR-swizzled by (row & 7) as the tensor map expects
-        const float inv = __fdividef(1.f, lsum);
-        uint8_t* srow = sO + rl * 128;
+      for (int v = 0; v < kD / 8; ++v) {
+        uint32_t w[4];
 #pragma unroll
-        for (int v = 0; v < kOC / 8; ++v) {
-          uint32_t w[4];
-#pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            __nv_bfloat162 tt = __floats2bfloat162_rn(o[8 * v + 2 * u] * inv, o[8 * v + 2 * u + 1] * inv);
-            w[u] = *reinterpret_cast<uint32_t*>(&tt);
-          }
-          const int chunk = (part * kOC) / 8 + v;
-          *reinterpret_cast<uint4*>(srow + ((chunk ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        for (int u = 0; u < 4; ++u) {
+          __nv_bfloat162 tt = __floats2bfloat162_rn(__uint_as_float(o[8 * v + 2 * u]) * inv,
+                                                    __uint_as_float(o[8 * v + 2 * u + 1]) * inv);
+          w[u] = *reinterpret_cast<uint32_t*>(&tt);
         }
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        softmax_bar();
-        if (tid == 0 && ok) {  // rows past T are clipped by the tensor map
-          tma_store_4d(&to, smem_addr(sO), 0, c.h, c.qb * kRows, c.b);
-          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-        }
-        (void)row;
+        *reinterpret_cast<uint4*>(srow + ((v ^ (rl & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      wg_bar(pipe);
+      if (rl == 0 && ok) {   // rows past T are clipped by the tensor map
+        tma_store_4d(&to, smem_addr(sO), 0, c.h, c.qb * kRows, c.b);
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       }
     }
+    if (rl == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output tiles written
   }
-  if (tid == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output tiles written
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512u));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot), "r"(512u));
   }
 }
 
@@ -466,17 +456,14 @@ int launch(const void* q, const void* k, const void* v, void* out, int64_t B, in
   p.T = (int)T;
   p.n_qblk = (int)((T + kRows - 1) / kRows);
   p.scale_log2 = scale_log2;
-  p.out = (__nv_bfloat16*)out;
-  p.osb = os[0];
-  p.osh = os[1];
-  p.ost = os[2];
   const int64_t tiles = B * H * p.n_qblk;
   if (tiles > 0x7fffffff) return fail(GPT_ERR_UNSUPPORTED, "attention work too large");
   p.BH = (int)(B * H);
   p.n_tiles = (int)tiles;
   int sms = device_sm_count();
   if (sms <= 0) sms = 148;
-  const int grid = (int)(tiles < sms ? tiles : sms);   // persistent: one CTA per SM
+  const int64_t pairs = (tiles + kPipes - 1) / kPipes;
+  const int grid = (int)(pairs < sms ? pairs : sms);   // persistent: one CTA per SM, two tiles in flight
   launch_pdl(attn_tc_kernel, dim3((unsigned)grid), dim3(kThreads), kSmem, st, mq, mk, mv, mo, p);
   return launch_status("attention_tc");
 }

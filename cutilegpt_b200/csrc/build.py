@@ -15,7 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 PKG = os.path.dirname(HERE)
 LIB_DIR = os.path.join(PKG, "lib")
 LIB_PATH = os.path.join(LIB_DIR, "libgpt_b200.so")
-SOURCES = ["libgpt_b200.cu", "common.cuh", "capi.cu", "elementwise.cu", "gemm_tc.cu", "gemm_skinny.cu",
+SOURCES = ["libgpt_b200.cu", "common.cuh", "capi.cu", "elementwise.cu", "gemm_tc.cu", "gemm_skinny.cu", "gemm_rows.cu",
            "gemm_simt.cu", "attention_tc.cu", "attention.cu", "decode.cu", "decode_noalloc.cu",
            "sampling.cu"]
 HEADER = os.path.join(os.path.dirname(PKG), "include", "gpt_b200.h")

@@ -167,7 +167,7 @@ extern "C" int gpt_gemm_fused(const void* A, int64_t lda, const void* W, const v
   if (f.ln_stats) {
     GPT_CHECK_ARG(f.ln_u && f.ln_v && f.ln_parts >= 1 && f.ln_eps >= 0.f, "gpt_gemm_fused: incomplete LayerNorm fold");
     GPT_CHECK_ARG(epilogue != GPT_EPI_BIAS_RESIDUAL, "gpt_gemm_fused: LayerNorm fold with a residual epilogue");
-  } else {
+  } else if (!f.ln_sums) {
     GPT_CHECK_ARG(epilogue == GPT_EPI_NONE || bias, "gpt_gemm_fused: epilogue needs bias");
   }
   if (f.k_cache || f.v_cache) {
@@ -175,8 +175,22 @@ extern "C" int gpt_gemm_fused(const void* A, int64_t lda, const void* W, const v
                   "gpt_gemm_fused: incomplete KV append");
     GPT_CHECK_SHAPE(N == 3 * f.kv_heads * f.kv_dim, "gpt_gemm_fused: KV append needs N = 3 * heads * dim");
   }
+  GPT_CHECK_ARG(!(f.ln_stats && f.ln_sums), "gpt_gemm_fused: give ln_stats or ln_sums, not both");
+  if (f.ln_sums)
+    GPT_CHECK_ARG(f.ln_u && f.ln_v && f.ln_eps >= 0.f && epilogue != GPT_EPI_BIAS_RESIDUAL,
+                  "gpt_gemm_fused: incomplete LayerNorm fold");
   GPT_CHECK_ARG(gpt::tc::tc_eligible(A, lda, W, K, M, N),
                 "gpt_gemm_fused: operands must be 16-byte aligned with 16-byte row pitches");
+  // Exact fp64 row sums (and, with them, the KV append) run on the 16-column decode GEMM.
+  if (f.row_sums || (f.ln_sums && gpt::tc::rows_eligible(A, lda, W, C, ldc, M, N, K))) {
+    GPT_CHECK_ARG(!f.ln_stats && !f.row_stats, "gpt_gemm_fused: fp32 parts and fp64 sums cannot be mixed");
+    GPT_CHECK_SHAPE(gpt::tc::rows_eligible(A, lda, W, C, ldc, M, N, K),
+                    "gpt_gemm_fused: row_sums need M <= 128 and N %% 16 == 0 (M=%lld N=%lld)", (long long)M,
+                    (long long)N);
+    return gpt::tc::gemm_rows(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, &f, (cudaStream_t)stream);
+  }
+  GPT_CHECK_ARG(!f.ln_sums || M <= gpt::tc::kSkMaxM, "gpt_gemm_fused: ln_sums serve at most %d rows",
+                gpt::tc::kSkMaxM);
   if (M <= gpt::tc::kSkMaxM)
     return gpt::tc::gemm_skinny_fused(A, lda, W, bias, R, ldr, C, ldc, M, N, K, epilogue, f, (cudaStream_t)stream);
   // more rows (prefill): the tcgen05 GEMM with the LayerNorm fold or row statistics

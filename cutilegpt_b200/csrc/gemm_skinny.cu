@@ -41,6 +41,7 @@ struct SkParams {
   const __nv_bfloat16* W;  // [N][K] (row pitch K): L2 prefetch of the slice past the ring
   // Fused decode extras (gemm_skinny_kernel<EPI, true> only; each may be null):
   const float* ln_stats;  // [ln_parts][M][2] (sum, sum of squares) of A's rows: LayerNorm folded in
+  const double* ln_sums;  // or [M][2] fp64 totals of the same (one part)
   const float* ln_u;      // [N] row sums of the gamma-scaled weight
   const float* ln_v;      // [N] W . beta + bias (replaces bias)
   int ln_parts;
@@ -52,6 +53,24 @@ struct SkParams {
   int64_t kv_tmax, kv_pos0;
   const int64_t* kv_pos;
 };
+
+// mean / rstd of row m for the LayerNorm fold, from fp64 totals or fp32 per-part sums.
+__device__ __forceinline__ void sk_ln_row(const SkParams& p, int m, float& mean, float& rstd) {
+  if (p.ln_sums) {
+    const double2 s = *reinterpret_cast<const double2*>(p.ln_sums + 2 * (int64_t)m);
+    const double mu = s.x * (double)p.ln_inv_k;
+    mean = (float)mu;
+    rstd = rsqrtf((float)fmax(s.y * (double)p.ln_inv_k - mu * mu, 0.0) + p.ln_eps);
+    return;
+  }
+  float s1 = 0.f, s2 = 0.f;
+  for (int q = 0; q < p.ln_parts; ++q) {
+    s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
+    s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
+  }
+  mean = s1 * p.ln_inv_k;
+  rstd = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
+}
 
 template <int EPI>
 __device__ __forceinline__ void sk_store(const SkParams& p, int m, int n, float v) {
@@ -235,21 +254,13 @@ __global__ void __launch_bounds__(kSkThreads, 4)
       // LayerNorm folded in (the host allows no other extra without split-K):
       // row statistics of all Mp rows into shared memory first.
       __shared__ float ln_ms[kSkMaxM][2];
-      if (p.ln_stats) {
-        for (int m = threadIdx.x; m < p.M; m += kSkThreads) {
-          float s1 = 0.f, s2 = 0.f;
-          for (int q = 0; q < p.ln_parts; ++q) {
-            s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
-            s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
-          }
-          const float mean = s1 * p.ln_inv_k;
-          ln_ms[m][0] = mean;
-          ln_ms[m][1] = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
-        }
+      const bool lnf = p.ln_stats || p.ln_sums;
+      if (lnf) {
+        for (int m = threadIdx.x; m < p.M; m += kSkThreads) sk_ln_row(p, m, ln_ms[m][0], ln_ms[m][1]);
       }
       __syncthreads();
-      const float un = (p.ln_stats && n_ok) ? p.ln_u[n] : 0.f;
-      const float vn = (p.ln_stats && n_ok) ? p.ln_v[n] : 0.f;
+      const float un = (lnf && n_ok) ? p.ln_u[n] : 0.f;
+      const float vn = (lnf && n_ok) ? p.ln_v[n] : 0.f;
       for (int c = 0; c < p.Mp && ok; c += 32) {
         uint32_t r[32];
         tmem_ld32(lane_base + (uint32_t)c, r);
@@ -258,7 +269,7 @@ __global__ void __launch_bounds__(kSkThreads, 4)
           const int m = c + j;
           if (m < p.M && n_ok) {
             float x = __uint_as_float(r[j]);
-            if (p.ln_stats) x = ln_ms[m][1] * (x - ln_ms[m][0] * un) + vn;
+            if (lnf) x = ln_ms[m][1] * (x - ln_ms[m][0] * un) + vn;
             else if (EPI != GPT_EPI_NONE) x += __bfloat162float(p.bias[n]);
             if (EPI == GPT_EPI_BIAS_GELU) x = gelu_tanh<true>(x);
             if (EPI == GPT_EPI_BIAS_RESIDUAL) x += __bfloat162float(p.resid[(int64_t)m * p.ldr + n]);
@@ -289,7 +300,7 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     // Bias (or the LayerNorm fold's u / v) of these columns, and the residual
     // of the first row, fetched while the partials are still being produced.
     float b4[4] = {0.f, 0.f, 0.f, 0.f}, u4[4] = {0.f, 0.f, 0.f, 0.f};
-    const bool ln = kFuse && p.ln_stats != nullptr;
+    const bool ln = kFuse && (p.ln_stats != nullptr || p.ln_sums != nullptr);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       if (e < ncnt) {
@@ -311,17 +322,8 @@ __global__ void __launch_bounds__(kSkThreads, 4)
     // producer's per-tile partials (published by the barrier before the push).
     __shared__ float ln_ms[64][2];
     if constexpr (kFuse) {
-      if (ln && (int)threadIdx.x < r_cnt && r_lo + (int)threadIdx.x < p.M) {
-        const int m = r_lo + threadIdx.x;
-        float s1 = 0.f, s2 = 0.f;
-        for (int q = 0; q < p.ln_parts; ++q) {
-          s1 += p.ln_stats[((int64_t)q * p.M + m) * 2];
-          s2 += p.ln_stats[((int64_t)q * p.M + m) * 2 + 1];
-        }
-        const float mean = s1 * p.ln_inv_k;
-        ln_ms[threadIdx.x][0] = mean;
-        ln_ms[threadIdx.x][1] = rsqrtf(fmaxf(s2 * p.ln_inv_k - mean * mean, 0.f) + p.ln_eps);
-      }
+      if (ln && (int)threadIdx.x < r_cnt && r_lo + (int)threadIdx.x < p.M)
+        sk_ln_row(p, r_lo + threadIdx.x, ln_ms[threadIdx.x][0], ln_ms[threadIdx.x][1]);
     }
     const bool ok = mbar_wait(smem_addr(done), 0);
     tc_fence_after();
@@ -617,6 +619,7 @@ int gemm_skinny_fused(const void* A, int64_t lda, const void* W, const void* bia
   p.ldc = ldc;
   p.vec_c = aligned(C, 8) && ldc % 4 == 0;
   p.ln_stats = f.ln_stats;
+  p.ln_sums = f.ln_sums;
   p.ln_u = f.ln_u;
   p.ln_v = f.ln_v;
   p.ln_parts = (int)f.ln_parts;

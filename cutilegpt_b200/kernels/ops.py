@@ -83,10 +83,12 @@ def gemm_fused(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.
                row_stats: torch.Tensor | None = None, kv=None) -> torch.Tensor:
     """Few-row (decode) GEMM with fused extras, bf16, M <= 256.
 
-    ln = (stats [parts, M, 2] fp32, eps, u [N] fp32, v [N] fp32): LayerNorm folded in, `w` being the
-    gamma-scaled weight from lnfold_weights; row_stats [ceil(N/128), M, 2] fp32 receives the
-    per-tile (sum, sum of squares) of the stored rows; kv = (k_cache, v_cache [B, H, Tmax, D],
-    pos_dev int64 [1] or None, pos0) appends the k / v parts of a fused QKV output.
+    ln = (stats, eps, u [N] fp32, v [N] fp32): LayerNorm folded in, `w` being the gamma-scaled
+    weight from lnfold_weights; stats is either fp64 [M, 2] exact row totals or fp32 [parts, M, 2]
+    per-tile sums. row_stats fp64 [M, 2] is added to with the (sum, sum of squares) of the stored
+    rows (the 16-column decode GEMM); fp32 [ceil(N/128), M, 2] receives per-tile sums instead.
+    kv = (k_cache, v_cache [B, H, Tmax, D], pos_dev int64 [1] or None, pos0) appends the k / v
+    parts of a fused QKV output.
     """
     M, K = a.shape
     N = w.shape[0]
@@ -98,9 +100,16 @@ def gemm_fused(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor, bias: torch.
     f = L.GemmFusion()
     if ln is not None:
         stats, eps, u, v = ln
-        f.ln_stats, f.ln_parts, f.ln_eps, f.ln_u, f.ln_v = _ptr(stats), stats.shape[0], float(eps), _ptr(u), _ptr(v)
+        f.ln_eps, f.ln_u, f.ln_v = float(eps), _ptr(u), _ptr(v)
+        if stats.dtype == torch.float64:         # exact row totals [M, 2]
+            f.ln_sums = _ptr(stats)
+        else:                                    # fp32 per-tile parts [parts, M, 2]
+            f.ln_stats, f.ln_parts = _ptr(stats), stats.shape[0]
     if row_stats is not None:
-        f.row_stats = _ptr(row_stats)
+        if row_stats.dtype == torch.float64:     # [M, 2], accumulated into
+            f.row_sums = _ptr(row_stats)
+        else:
+            f.row_stats = _ptr(row_stats)
     if kv is not None:
         kc, vc, pos_dev, pos0 = kv
         _, H, Tmax, D = kc.shape
@@ -121,6 +130,16 @@ def row_stats(x: torch.Tensor, stats: torch.Tensor) -> torch.Tensor:
     L.check(L.lib().gpt_row_stats(_ptr(x), _row_stride(x, "row_stats"), M, C, _ptr(stats), L.dtype_code(x.dtype),
                                   L.stream_ptr()), "gpt_row_stats")
     return stats
+
+
+def row_sums(x: torch.Tensor, sums: torch.Tensor, zero: torch.Tensor | None = None) -> torch.Tensor:
+    """sums fp64 [M, 2] <- (sum, sum of squares) of each row of x [M, C]; `zero` (fp64, any shape,
+    contiguous) is cleared in the same launch."""
+    M, C = x.shape
+    nz = zero.numel() if zero is not None else 0
+    L.check(L.lib().gpt_row_sums(_ptr(x), _row_stride(x, "row_sums"), M, C, _ptr(sums), _ptr(zero), nz,
+                                 L.dtype_code(x.dtype), L.stream_ptr()), "gpt_row_sums")
+    return sums
 
 
 def lnfold_weights(w: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, bias: torch.Tensor | None):

@@ -81,11 +81,12 @@ class _DecodeState:
         self.seed = torch.zeros((1,), dtype=torch.int64, device=device)   # RNG seed of the sampling kernel
         # folded decode step: bf16, up to 128 rows (the split-K receive buffers of the fused GEMMs
         # fit shared memory up to there), 16-byte row pitches for the TMA operands
-        self.fold = (fold and dtype == torch.bfloat16 and 1 <= B <= 128 and C % 8 == 0
+        self.fold = (fold and dtype == torch.bfloat16 and 1 <= B <= 128 and C % 16 == 0 and D % 16 == 0
                      and cfg.n_layer >= 1)
         if self.fold:
-            parts = (C + 127) // 128
-            self.stats = torch.zeros((2 * cfg.n_layer + 1, parts, B, 2), dtype=torch.float32, device=device)
+            # exact fp64 row totals (sum, sum of squares) of the residual stream: slot 2i = rows entering
+            # block i, 2i+1 = after its attention, 2L = entering ln_f; slots >= 1 are accumulated into
+            self.sums = torch.zeros((2 * cfg.n_layer + 1, B, 2), dtype=torch.float64, device=device)
 
 
 class CutileGPT:
@@ -354,29 +355,26 @@ class CutileGPT:
         ops.embedding_pos(st.tok.view(B, 1), self._w('wte'), self._w('wpe'), st.x, pos0=0, pos_dev=st.pos)
         q = st.qkv[:, :C]
         if st.fold:
-            # LayerNorms folded into the GEMMs that follow them; statistics slot 2i holds the rows
-            # entering block i (parts: 1 from the embedding, then one per 128-column tile of the
-            # residual GEMMs), slot 2i+1 the rows after its attention.
+            # LayerNorms folded into the GEMMs that follow them (exact fp64 row sums, see _DecodeState);
+            # the first launch writes slot 0 and clears the accumulators of the others.
             F = self._fold_weights()
             eps = 1e-5
-            ops.row_stats(st.x, st.stats[0, :1])
+            ops.row_sums(st.x, st.sums[0], zero=st.sums[1:])
             for i in range(cfg.n_layer):
                 p = f'h.{i}.'
-                s_in = st.stats[2 * i, :1] if i == 0 else st.stats[2 * i]
                 wf, u, v = F[p + 'attn']
-                ops.gemm_fused(st.x, wf, st.qkv, epilogue=L.EPI_BIAS, ln=(s_in, eps, u, v),
+                ops.gemm_fused(st.x, wf, st.qkv, epilogue=L.EPI_BIAS, ln=(st.sums[2 * i], eps, u, v),
                                kv=(st.cache[i, 0], st.cache[i, 1], st.pos, 0))
                 ops.attention_decode(q, st.cache[i, 0], st.cache[i, 1], st.att, 1, st.dec_ws, scale,
                                      len_dev=st.pos)
                 ops.gemm_fused(st.att, self._w(p + 'attn.c_proj.weight'), st.x, bias=self._w(p + 'attn.c_proj.bias'),
-                               resid=st.x, row_stats=st.stats[2 * i + 1])
+                               resid=st.x, row_stats=st.sums[2 * i + 1])
                 wf, u, v = F[p + 'fc']
-                ops.gemm_fused(st.x, wf, st.f, epilogue=L.EPI_BIAS_GELU, ln=(st.stats[2 * i + 1], eps, u, v))
+                ops.gemm_fused(st.x, wf, st.f, epilogue=L.EPI_BIAS_GELU, ln=(st.sums[2 * i + 1], eps, u, v))
                 ops.gemm_fused(st.f, self._w(p + 'mlp.c_proj.weight'), st.x, bias=self._w(p + 'mlp.c_proj.bias'),
-                               resid=st.x, row_stats=st.stats[2 * i + 2])
+                               resid=st.x, row_stats=st.sums[2 * i + 2])
             wf, u, v = F['lm']
-            s_in = st.stats[2 * cfg.n_layer, :1] if cfg.n_layer == 0 else st.stats[2 * cfg.n_layer]
-            ops.gemm_fused(st.x, wf, st.logits, epilogue=L.EPI_NONE, ln=(s_in, eps, u, v))
+            ops.gemm_fused(st.x, wf, st.logits, epilogue=L.EPI_NONE, ln=(st.sums[2 * cfg.n_layer], eps, u, v))
             return
         for i in range(cfg.n_layer):
             p = f'h.{i}.'

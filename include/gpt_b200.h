@@ -210,7 +210,16 @@ GPT_API int gpt_argmax(const void* logits, int64_t ld, int64_t B, int64_t V,
  *  - k_cache / v_cache: the output is the fused QKV row [q | k | v] of
  *    kv_heads x kv_dim each; its k and v parts are also written to the caches
  *    [M][kv_heads][kv_tmax][kv_dim] at position kv_pos0 + *kv_pos_dev
- *    (replaces gpt_kv_append). */
+ *    (replaces gpt_kv_append).
+ *  - ln_sums / row_sums: the same two extras with exact fp64 row totals
+ *    instead of fp32 per-tile parts: ln_sums [M][2] (sum, sum of squares of
+ *    each row of x over K) feeds the LayerNorm fold (ln_stats must then be
+ *    NULL); row_sums [M][2] is ADDED to (atomically, in fp64, order-free
+ *    because the terms are exact) with the (sum, sum of squares) of every
+ *    stored output row, so it must hold zeros first (gpt_row_sums clears a
+ *    step's worth). With M <= 128, N % 16 == 0 and 16 | kv_dim these run on
+ *    the decode-step GEMM with 16-column tiles (gemm_rows); ln_sums alone
+ *    also works with any N on M <= 256 (the lm_head). */
 typedef struct gpt_gemm_fusion {
   const float* ln_stats;
   int64_t ln_parts;
@@ -225,12 +234,22 @@ typedef struct gpt_gemm_fusion {
   int64_t kv_tmax;
   int64_t kv_pos0;
   const int64_t* kv_pos_dev;
+  const double* ln_sums;
+  double* row_sums;
 } gpt_gemm_fusion;
 
 GPT_API int gpt_gemm_fused(const void* A, int64_t lda, const void* W,
                const void* bias, const void* R, int64_t ldr, void* C,
                int64_t ldc, int64_t M, int64_t N, int64_t K, int epilogue,
                const gpt_gemm_fusion* fusion, int dtype, void* stream);
+
+/* Start of a folded decode step: sums[m] = (sum, sum of squares) over the
+ * C values of row m of x (row stride ld), in fp64 — the ln_sums of the
+ * first folded GEMM — and zero[0 .. n_zero) cleared (the row_sums
+ * accumulators of the step's later GEMMs). One launch. */
+GPT_API int gpt_row_sums(const void* x, int64_t ld, int64_t M, int64_t C,
+               double* sums, double* zero, int64_t n_zero, int dtype,
+               void* stream);
 
 /* (sum, sum of squares) of each row of x [M, C] (row stride ld) ->
  * stats [1][M][2]: the ln_stats of a folded GEMM that reads the embedding

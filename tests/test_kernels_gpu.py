@@ -459,3 +459,97 @@ def test_gemm_qkv_kv_append(B, H):
     assert kc.abs().sum().item() == 0 and vc.abs().sum().item() == 0   # nothing else touched
     with pytest.raises(ValueError):
         ops.gemm_fused(x, w[:100], qkv[:, :100], bias=bias[:100], kv=(kc, vc, pos, 0))   # N != 3 * H * D
+
+
+# ----------------------------------------------------------------- 16-column decode GEMM (exact fp64 row sums)
+@pytest.mark.parametrize("M,C,N,epi", [(64, 768, 2304, L.EPI_BIAS), (64, 768, 3072, L.EPI_BIAS_GELU),
+                                       (1, 768, 2304, L.EPI_BIAS), (100, 1600, 4800, L.EPI_BIAS),
+                                       (128, 768, 3072, L.EPI_BIAS_GELU), (7, 384, 1536, L.EPI_BIAS_GELU)])
+def test_rows_gemm_layernorm_fold_fp64_sums(M, C, N, epi):
+    """LayerNorm folded in with exact fp64 row totals (gpt_row_sums) equals LayerNorm then Linear."""
+    dt = torch.bfloat16
+    x = (randn(M, C, seed=90, scale=2.0) + 0.7).to(dt)
+    g = (randn(C, seed=91) * 0.2 + 1.0).to(dt)
+    b = (randn(C, seed=92) * 0.2).to(dt)
+    w = (randn(N, C, seed=93) / math.sqrt(C)).to(dt)
+    bias = randn(N, seed=94).to(dt)
+    xc = x.cuda()
+    wf, u, v = ops.lnfold_weights(w.cuda(), g.cuda(), b.cuda(), bias.cuda())
+    sums = torch.full((M, 2), float("nan"), dtype=torch.float64, device="cuda")
+    zero = torch.full((3, M, 2), 5.0, dtype=torch.float64, device="cuda")
+    ops.row_sums(xc, sums, zero=zero)
+    xd = x.double()
+    torch.testing.assert_close(sums.cpu(), torch.stack([xd.sum(-1), (xd ** 2).sum(-1)], -1), rtol=0, atol=1e-9)
+    assert zero.abs().sum().item() == 0
+    out = torch.empty((M, N), dtype=dt, device="cuda")
+    ops.gemm_fused(xc, wf, out, epilogue=epi, ln=(sums, 1e-5, u, v))
+    ref = R.layer_norm(xd, g.double(), b.double()) @ w.double().t() + bias.double()
+    if epi == L.EPI_BIAS_GELU:
+        ref = R.gelu(ref)
+    assert rel_err(out, ref) < BF16_REL, rel_err(out, ref)
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 768, 768), (64, 768, 3072), (100, 1600, 6400), (7, 768, 3072),
+                                   (128, 768, 768), (1, 1600, 1600)])
+def test_rows_gemm_residual_row_sums_split_k(M, N, K):
+    """Residual epilogue in place (C is R) over split-K clusters; fp64 row sums of the stored rows are
+    accumulated into what the buffer held (exact, so equal to the fp64 sums of the output + the start)."""
+    dt = torch.bfloat16
+    a, w = randn(M, K, seed=95).to(dt).cuda(), (randn(N, K, seed=96) / math.sqrt(K)).to(dt).cuda()
+    bias, x = randn(N, seed=97).to(dt).cuda(), randn(M, N, seed=98).to(dt).cuda()
+    x0 = x.double().cpu()
+    sums = torch.zeros((M, 2), dtype=torch.float64, device="cuda")
+    sums[:, 0] = 3.0
+    ops.gemm_fused(a, w, x, bias=bias, resid=x, row_stats=sums)
+    ref = a.double().cpu() @ w.double().cpu().t() + bias.double().cpu() + x0
+    assert rel_err(x, ref) < BF16_REL, rel_err(x, ref)
+    o = x.double().cpu()
+    torch.testing.assert_close(sums[:, 0].cpu(), o.sum(-1) + 3.0, rtol=0, atol=1e-9)
+    torch.testing.assert_close(sums[:, 1].cpu(), (o ** 2).sum(-1), rtol=0, atol=1e-9)
+    # deterministic: the same call on the same inputs gives bit-identical outputs and sums
+    x2 = x0.to(dt).cuda()
+    s2 = torch.zeros((M, 2), dtype=torch.float64, device="cuda")
+    s2[:, 0] = 3.0
+    ops.gemm_fused(a, w, x2, bias=bias, resid=x2, row_stats=s2)
+    assert torch.equal(x2, x) and torch.equal(s2, sums)
+
+
+@pytest.mark.parametrize("B,H", [(64, 12), (3, 25), (128, 12)])
+def test_rows_gemm_qkv_kv_append_with_fold(B, H):
+    """The folded QKV GEMM writes q|k|v and appends k, v at the device position (16-column kernel)."""
+    dt, D, Tmax = torch.bfloat16, 64, 40
+    C = H * D
+    x = randn(B, C, seed=99).to(dt).cuda()
+    g, b = (randn(C, seed=100) * 0.1 + 1).to(dt).cuda(), (randn(C, seed=101) * 0.1).to(dt).cuda()
+    w, bias = (randn(3 * C, C, seed=102) / math.sqrt(C)).to(dt).cuda(), randn(3 * C, seed=103).to(dt).cuda()
+    wf, u, v = ops.lnfold_weights(w, g, b, bias)
+    sums = torch.empty((B, 2), dtype=torch.float64, device="cuda")
+    ops.row_sums(x, sums)
+    kc = torch.zeros((B, H, Tmax, D), dtype=dt, device="cuda")
+    vc = torch.zeros_like(kc)
+    pos = torch.tensor([17], dtype=torch.int64, device="cuda")
+    qkv = torch.empty((B, 3 * C), dtype=dt, device="cuda")
+    ops.gemm_fused(x, wf, qkv, epilogue=L.EPI_BIAS, ln=(sums, 1e-5, u, v), kv=(kc, vc, pos, 2))
+    ref = R.layer_norm(x.double().cpu(), g.double().cpu(), b.double().cpu()) @ w.double().cpu().t() \
+        + bias.double().cpu()
+    assert rel_err(qkv, ref) < BF16_REL
+    q3 = qkv.view(B, 3, H, D).cpu()
+    assert torch.equal(kc[:, :, 19].cpu(), q3[:, 1]) and torch.equal(vc[:, :, 19].cpu(), q3[:, 2])
+    kc[:, :, 19] = 0
+    vc[:, :, 19] = 0
+    assert kc.abs().sum().item() == 0 and vc.abs().sum().item() == 0
+
+
+def test_rows_gemm_lm_head_fold_any_n():
+    """ln_f folded into a head whose N is not a multiple of 16 (fp64 totals on the few-row kernel)."""
+    dt, M, C, N = torch.bfloat16, 64, 768, 50257
+    x = randn(M, C, seed=104, scale=1.5).to(dt).cuda()
+    g, b = (randn(C, seed=105) * 0.1 + 1).to(dt).cuda(), (randn(C, seed=106) * 0.1).to(dt).cuda()
+    w = (randn(N, C, seed=107) / math.sqrt(C)).to(dt).cuda()
+    wf, u, v = ops.lnfold_weights(w, g, b, None)
+    sums = torch.empty((M, 2), dtype=torch.float64, device="cuda")
+    ops.row_sums(x, sums)
+    out = torch.empty((M, N), dtype=dt, device="cuda")
+    ops.gemm_fused(x, wf, out, epilogue=L.EPI_NONE, ln=(sums, 1e-5, u, v))
+    ref = R.layer_norm(x.double().cpu(), g.double().cpu(), b.double().cpu()) @ w.double().cpu().t()
+    assert rel_err(out, ref) < BF16_REL
