@@ -564,9 +564,9 @@ def run_probe(name, local):
 
 # Per-launch DRAM traffic of the GEMM family in one cfg-3 step, from one ncu capture of the full-size
 # bench step (dram__bytes_read.sum + dram__bytes_write.sum over the gemm_tc_kernel launches of one
-# step, divided by their count); the command and the per-kernel table are in
-# profiles/gemm_tc_cfg3_dram.md. None until that capture exists.
-GEMM_TRAFFIC_BYTES_PER_LAUNCH = None
+# step, divided by their count: 5723 MB over 49 launches). The block GEMMs read less than their
+# algorithmic bytes because their activations are still in L2; the lm_head writes its logits once.
+GEMM_TRAFFIC_BYTES_PER_LAUNCH = 116.8e6
 
 
 def main():
