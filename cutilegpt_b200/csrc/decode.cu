@@ -15,6 +15,10 @@ namespace gpt {
 namespace dec {
 
 constexpr int kWarps = 4;
+// Resident CTAs per SM the register budget must allow: the cfg-4 grid (64 x 12
+// (b, h) pairs, one split) then runs as a single wave on 148 SMs instead of
+// 1.04 waves at the 5 CTAs per SM that 92 registers per thread allow.
+constexpr int kMinBlocks = 6;
 constexpr float kLog2e = 1.4426950408889634f;
 
 // Number of KV splits: enough CTAs to cover the SMs twice, at least 64
@@ -31,7 +35,7 @@ inline int num_splits(int64_t B, int64_t H, int64_t L, int sms) {
 }
 
 template <typename T, int D>
-__global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict__ q, int64_t ld_q,
+__global__ void __launch_bounds__(kWarps * 32, kMinBlocks) decode_kernel(const T* __restrict__ q, int64_t ld_q,
                                                              const T* __restrict__ kc,
                                                              const T* __restrict__ vc, T* __restrict__ out,
                                                              int64_t ld_out, int H, int64_t Tmax, int L0,
@@ -99,11 +103,13 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict
   // 2 x kUnroll 16-byte loads in flight; the running max is updated once per
   // step.
   constexpr int kUnroll = 8;
-  for (int j0 = c0 + warp * KPW * kUnroll; j0 < c1; j0 += kWarps * KPW * kUnroll) {
+  // Key group g (KPW keys) of the chunk belongs to warp g % kWarps, so the
+  // warps of a CTA issue equal numbers of loads.
+  for (int j0 = c0 + warp * KPW; j0 < c1; j0 += kWarps * KPW * kUnroll) {
     uint4 kr[kUnroll], vr[kUnroll];
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
-      const int j = j0 + u * KPW + grp;
+      const int j = j0 + u * kWarps * KPW + grp;
       kr[u] = make_uint4(0, 0, 0, 0);
       vr[u] = make_uint4(0, 0, 0, 0);
       if (j < c1) {
@@ -124,7 +130,7 @@ __global__ void __launch_bounds__(kWarps * 32) decode_kernel(const T* __restrict
     for (int u = 0; u < kUnroll; ++u) {
 #pragma unroll
       for (int o = 1; o < LPK; o <<= 1) dot[u] += __shfl_xor_sync(0xffffffffu, dot[u], o);
-      if (j0 + u * KPW + grp >= c1) dot[u] = -INFINITY;  // masked key
+      if (j0 + u * kWarps * KPW + grp >= c1) dot[u] = -INFINITY;  // masked key
     }
     float mx = dot[0];
 #pragma unroll
