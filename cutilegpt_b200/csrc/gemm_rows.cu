@@ -382,10 +382,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (ok && got) store_unit<EPI>(p, um, n0, acc, in);
     }
   }
-  // No CTA leaves while a peer may still write into its shared memory.
-  if (clustered) {
-    asm volatile("barrier.cluster.arrive.release.aligned;\nbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-  }
+  // No closing cluster barrier: every write into this CTA's shared memory is
+  // a partial counted on its receive barrier, which it has waited for, so no
+  // peer can still be writing here when it leaves.
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
