@@ -505,7 +505,7 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
               const float2 bf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&bw[j]));
               v0 += bf.x; v1 += bf.y;
             }
-            if (EPI == GPT_EPI_BIAS_GELU) { v0 = gelu_tanh<true>(v0); v1 = gelu_tanh<true>(v1); }
+            if (EPI == GPT_EPI_BIAS_GELU) gelu_tanh2_fast(v0, v1);
             if (EPI == GPT_EPI_BIAS_RESIDUAL) {
               const float2 rf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rw[j]));
               v0 += rf.x; v1 += rf.y;
