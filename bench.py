@@ -34,6 +34,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -517,6 +518,81 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_decode_parts(local):
+    """Config-4 decode step (GPT-2 124M, B64, cached length 193) taken apart: each part is the same kernel
+    sequence the folded step launches (one launch per layer), captured in a CUDA graph 4 times over and
+    replayed 20 times, timed with CUDA events; us = per replay of one part sequence. Prints one JSON line."""
+    from cutilegpt_b200 import CutileGPT, GPTConfig
+    from cutilegpt_b200 import _lib as L
+    from cutilegpt_b200.kernels import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = GPTConfig(n_layer=12, n_head=12, n_embd=768, vocab_size=50257, block_size=1024)
+    m = CutileGPT(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+    B, P, S = 64, 128, 128
+    prompt = torch.randint(0, cfg.vocab_size, (B, P), generator=torch.Generator().manual_seed(1)).to(dev)
+    m.generate(prompt, 16, top_k=1)
+    st = m._decode_state(B, P + S)
+    F = m._fold_weights()
+    C, H, eps = cfg.n_embd, cfg.n_head, 1e-5
+    scale = 1.0 / math.sqrt(C // H)
+    q = st.qkv[:, :C]
+
+    def qkv(i):
+        wf, u, v = F[f"h.{i}.attn"]
+        ops.gemm_fused(st.x, wf, st.qkv, epilogue=L.EPI_BIAS, ln=(st.sums[2 * i], eps, u, v),
+                       kv=(st.cache[i, 0], st.cache[i, 1], st.pos, 0))
+
+    def att(i):
+        ops.attention_decode(q, st.cache[i, 0], st.cache[i, 1], st.att, 1, st.dec_ws, scale, len_dev=st.pos)
+
+    def cproj(i):   # writes a scratch output (st.h) so the residual stream stays as it is
+        p = f"h.{i}."
+        ops.gemm_fused(st.att, m._w(p + "attn.c_proj.weight"), st.h, bias=m._w(p + "attn.c_proj.bias"),
+                       resid=st.x, row_stats=st.sums[2 * i + 1])
+
+    def fc(i):
+        wf, u, v = F[f"h.{i}.fc"]
+        ops.gemm_fused(st.x, wf, st.f, epilogue=L.EPI_BIAS_GELU, ln=(st.sums[2 * i + 1], eps, u, v))
+
+    def mproj(i):
+        p = f"h.{i}."
+        ops.gemm_fused(st.f, m._w(p + "mlp.c_proj.weight"), st.h, bias=m._w(p + "mlp.c_proj.bias"),
+                       resid=st.x, row_stats=st.sums[2 * i + 2])
+
+    def lm():
+        wf, u, v = F["lm"]
+        ops.gemm_fused(st.x, wf, st.logits, epilogue=L.EPI_NONE, ln=(st.sums[2 * cfg.n_layer], eps, u, v))
+        ops.argmax(st.logits, st.tok)
+
+    parts = {
+        "full_step": lambda: m._decode_step(st),
+        "qkv_x12": lambda: [qkv(i) for i in range(12)],
+        "attention_x12": lambda: [att(i) for i in range(12)],
+        "attn_c_proj_x12": lambda: [cproj(i) for i in range(12)],
+        "c_fc_x12": lambda: [fc(i) for i in range(12)],
+        "mlp_c_proj_x12": lambda: [mproj(i) for i in range(12)],
+        "lm_head_argmax": lm,
+        "row_sums_x12 (launch floor)": lambda: [ops.row_sums(st.x, st.sums[0]) for _ in range(12)],
+    }
+    out = {}
+    for name, fn in parts.items():
+        st.pos.fill_(192)
+        fn()
+        torch.cuda.synchronize()
+        g = m._capture_fn(lambda: [fn() for _ in range(4)])
+        for _ in range(3):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(20):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = round(e0.elapsed_time(e1) / 20 / 4 * 1e3, 2)
+    print(json.dumps({"probe": "decode_parts", "unit": "us per part sequence", "parts": out}), flush=True)
+
+
 def run_probe(name, local):
     """One HBM-bound kernel alone, at a size whose inputs exceed the 126 MB L2, timed with CUDA events
     (3 warm-up + 10 timed launches); the profiling command runs the same probe under ncu.
@@ -591,12 +667,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-xl", action="store_true", help="skip the config-5 (GPT-2 XL) extras")
     ap.add_argument("--decode-only", action="store_true", help="only the config-4 decode run (profiling)")
-    ap.add_argument("--probe", choices=["layernorm", "gelu", "decode_attn"], default=None,
+    ap.add_argument("--probe", choices=["layernorm", "gelu", "decode_attn", "decode_parts"], default=None,
                     help="time one HBM-bound kernel alone at a size larger than L2 (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.probe == "decode_parts":
+        run_decode_parts(int(os.environ.get("LOCAL_RANK", "0")))
+        return
     if args.probe:
         run_probe(args.probe, int(os.environ.get("LOCAL_RANK", "0")))
         return
