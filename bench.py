@@ -593,6 +593,71 @@ def run_decode_parts(local):
     print(json.dumps({"probe": "decode_parts", "unit": "us per part sequence", "parts": out}), flush=True)
 
 
+def run_prefill_parts(local):
+    """Config-3 prefill forward (GPT-2 124M, B32xT512) taken apart: each part is the kernel sequence the
+    forward launches for it (one launch per layer), captured in a CUDA graph twice over and replayed 10
+    times, timed with CUDA events; us = per replay of one part sequence, TF/s from its algorithmic FLOPs
+    (attention: the causal half). Prints one JSON line."""
+    from cutilegpt_b200 import CutileGPT, GPTConfig
+    from cutilegpt_b200.kernels import ops
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = GPTConfig(n_layer=12, n_head=12, n_embd=768, vocab_size=50257, block_size=1024)
+    m = CutileGPT(cfg, dtype=torch.bfloat16, device=dev, seed=0)
+    B, T = 32, 512
+    C, H, D, V, n = cfg.n_embd, cfg.n_head, cfg.n_embd // cfg.n_head, cfg.vocab_size, cfg.n_layer
+    M = B * T
+    idx = torch.randint(0, V, (B, T), generator=torch.Generator().manual_seed(1)).to(dev)
+    logits = torch.empty(M, V, dtype=torch.bfloat16, device=dev)
+    ws = m._workspace(B, T)
+    m._blocks(idx, ws)
+    m._lm_head(ws, logits)
+    qkv4 = ws.qkv.view(B, T, 3, H, D)
+    q, k, v = (qkv4[:, :, j].transpose(1, 2) for j in range(3))
+    att4 = ws.att.view(B, T, H, D).transpose(1, 2)
+    scratch = torch.empty_like(ws.x)
+
+    def w(i, s):
+        return m._w(f"h.{i}.{s}")
+    from cutilegpt_b200 import _lib as Lb
+    parts = {
+        "full_forward": (lambda: (m._blocks(idx, ws), m._lm_head(ws, logits)), 4.2028e12),
+        "layernorm_x25": (lambda: [ops.layernorm(ws.x, w(0, "ln_1.weight"), w(0, "ln_1.bias"), ws.h)
+                                   for _ in range(2 * n + 1)], 0.0),
+        "qkv_x12": (lambda: [m._gemm(ws.h, w(i, "attn.c_attn.weight"), ws.qkv, bias=w(i, "attn.c_attn.bias"))
+                             for i in range(n)], n * 2.0 * M * C * 3 * C),
+        "attention_x12": (lambda: [ops.attention_prefill(q, k, v, att4, 1.0 / math.sqrt(D)) for _ in range(n)],
+                          n * 2.0 * B * H * T * (T + 1) * D),
+        "attn_c_proj_x12": (lambda: [m._gemm(ws.att, w(i, "attn.c_proj.weight"), scratch,
+                                             bias=w(i, "attn.c_proj.bias"), resid=ws.x) for i in range(n)],
+                            n * 2.0 * M * C * C),
+        "c_fc_x12": (lambda: [m._gemm(ws.h, w(i, "mlp.c_fc.weight"), ws.f, bias=w(i, "mlp.c_fc.bias"),
+                                      epilogue=Lb.EPI_BIAS_GELU) for i in range(n)], n * 2.0 * M * C * 4 * C),
+        "mlp_c_proj_x12": (lambda: [m._gemm(ws.f, w(i, "mlp.c_proj.weight"), scratch,
+                                            bias=w(i, "mlp.c_proj.bias"), resid=ws.x) for i in range(n)],
+                           n * 2.0 * M * 4 * C * C),
+        "lm_head": (lambda: m._lm_head(ws, logits), 2.0 * M * C * V),
+    }
+    out = {}
+    for name, (fn, flop) in parts.items():
+        fn()
+        torch.cuda.synchronize()
+        g = m._capture_fn(lambda: [fn() for _ in range(2)])
+        for _ in range(2):
+            g.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(10):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / 10 / 2 * 1e3
+        out[name] = {"us": round(us, 1)}
+        if flop:
+            out[name]["TF/s"] = round(flop / us / 1e6, 1)
+    print(json.dumps({"probe": "prefill_parts", "unit": "us per part sequence", "parts": out}), flush=True)
+
+
 def run_probe(name, local):
     """One HBM-bound kernel alone, at a size whose inputs exceed the 126 MB L2, timed with CUDA events
     (3 warm-up + 10 timed launches); the profiling command runs the same probe under ncu.
@@ -667,12 +732,15 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-xl", action="store_true", help="skip the config-5 (GPT-2 XL) extras")
     ap.add_argument("--decode-only", action="store_true", help="only the config-4 decode run (profiling)")
-    ap.add_argument("--probe", choices=["layernorm", "gelu", "decode_attn", "decode_parts"], default=None,
+    ap.add_argument("--probe", choices=["layernorm", "gelu", "decode_attn", "decode_parts", "prefill_parts"], default=None,
                     help="time one HBM-bound kernel alone at a size larger than L2 (profiling)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.probe == "prefill_parts":
+        run_prefill_parts(int(os.environ.get("LOCAL_RANK", "0")))
+        return
     if args.probe == "decode_parts":
         run_decode_parts(int(os.environ.get("LOCAL_RANK", "0")))
         return

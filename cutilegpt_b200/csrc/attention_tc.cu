@@ -10,15 +10,17 @@
 // MMAs run while the other tile's softmax does its exponentials. Per key
 // block of 128:
 //   S = Q Kᵀ      tcgen05.mma M=128 N=128 K=64 -> TMEM (this pipeline's S)
-//   softmax       pass 1 reads S (4 x 32 columns) for the row max; pass 2
-//                 reads it again, P = 2^(S·scale - m) (ex2.approx), row sum,
+//   softmax       the thread's whole S row (128 columns) is read into
+//                 registers once, which frees S for the next block's QKᵀ at
+//                 once; row max, P = 2^(S·scale - m) (ex2.approx), row sum,
 //                 P packed bf16 into TMEM (tcgen05.st), masked keys -> 0
 //   O += P V      tcgen05.mma with A = P from TMEM, B = V MN-major from its
 //                 TMA tile, accumulating in TMEM across the tile's blocks
 // The running max m only moves when a block's max exceeds it by more than
 // 2^8 (log2 domain): then O in TMEM and the row sum are rescaled once;
 // otherwise P uses the stale m (values stay below 2^8), and the final O / l
-// is the same softmax. TMEM per pipeline: S 128 columns, P 64, O 64 (512 in
+// is the same softmax. K and V blocks have separate two-slot rings (a K slot
+// is released by the QKᵀ that read it, a V slot by the PV). TMEM per pipeline: S 128 columns, P 64, O 64 (512 in
 // all). Q, K, V arrive by TMA through 4-D tensor maps {D, H, T, B} built
 // from the caller's strides, so both the fused [B, T, 3C] QKV buffer and the
 // [B, H, T, D] layout are read in place; rows past T are zero-filled by TMA
@@ -83,6 +85,36 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Packed f32x2 arithmetic (sm_100): two lanes per instruction.
+__device__ __forceinline__ uint64_t pack_f2(float a, float b) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "f"(a), "f"(b));
+  return v;
+}
+__device__ __forceinline__ uint64_t pack_u2(uint32_t a, uint32_t b) {
+  uint64_t v;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(v) : "r"(a), "r"(b));
+  return v;
+}
+__device__ __forceinline__ void unpack_f2(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 // O += P V with P (bf16, M = 128 x K = 16 slice) read from TMEM.
 __device__ __forceinline__ void tc_mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
                                           uint32_t accum) {
@@ -103,6 +135,18 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
   tmem_st16(taddr, r);
   tmem_st16(taddr + 16, r + 16);
 }
+__device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t* r) {   // no wait::ld
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Named barrier of one softmax warpgroup (ids 1, 2).
 __device__ __forceinline__ void wg_bar(int pipe) {
@@ -151,9 +195,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* bars = (uint64_t*)(base + kPipes * kPipeBytes) + pipe * 24;
   uint64_t* q_full = bars;                         // 2 (TMA tx)
   uint64_t* q_empty = bars + 2;                    // 2 (commit after a tile's last S)
-  uint64_t* kv_full = bars + 4;                    // kKvStages (TMA tx)
-  uint64_t* kv_empty = bars + 4 + kKvStages;       // kKvStages (commit after PV)
-  uint64_t* s_full = bars + 4 + 2 * kKvStages;     // commit after S
+  uint64_t* k_full = bars + 4;                     // kKvStages (TMA tx)
+  uint64_t* k_empty = bars + 4 + kKvStages;        // kKvStages (commit after S)
+  uint64_t* v_full = bars + 4 + 2 * kKvStages;     // kKvStages (TMA tx)
+  uint64_t* v_empty = bars + 4 + 3 * kKvStages;    // kKvStages (commit after PV)
+  uint64_t* s_full = bars + 4 + 4 * kKvStages;     // commit after S
   uint64_t* s_free = s_full + 1;                   // softmax warps: S read
   uint64_t* p_full = s_full + 2;                   // softmax warps: P written (and O rescaled)
   uint64_t* o_full = s_full + 3;                   // commit after PV
@@ -163,8 +209,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   if (tid == 0) {
     for (int q = 0; q < kPipes; ++q) {
       uint64_t* bq = (uint64_t*)(base + kPipes * kPipeBytes) + q * 24;
-      for (int i = 0; i < 4 + 2 * kKvStages; ++i) mbar_init(smem_addr(&bq[i]), 1);
-      uint64_t* sf = bq + 4 + 2 * kKvStages;
+      for (int i = 0; i < 4 + 4 * kKvStages; ++i) mbar_init(smem_addr(&bq[i]), 1);
+      uint64_t* sf = bq + 4 + 4 * kKvStages;
       mbar_init(smem_addr(&sf[0]), 1);   // s_full
       mbar_init(smem_addr(&sf[1]), 4);   // s_free
       mbar_init(smem_addr(&sf[2]), 4);   // p_full
@@ -209,15 +255,22 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                       lc.b);
           ++ql;
         }
+        // K and V have separate rings: a K slot is free once its QKᵀ has run, well before the PV
+        // that frees the V slot, so the next K blocks arrive a softmax step earlier
         const int st = lg % kKvStages;
-        if (lg >= kKvStages && !mbar_wait(smem_addr(&kv_empty[st]), (uint32_t)(((lg / kKvStages) - 1) & 1))) {
+        const uint32_t par = (uint32_t)(((lg / kKvStages) - 1) & 1);
+        if (lg >= kKvStages && !mbar_wait(smem_addr(&k_empty[st]), par)) {
           ok = false;
           break;
         }
-        const uint32_t fb = smem_addr(&kv_full[st]);
-        mbar_expect_tx(fb, 2 * kTileBytes);
-        tma_load_4d(smem_addr(sK + st * kTileBytes), &tk, fb, 0, lc.h, lc.j * kKeys, lc.b);
-        tma_load_4d(smem_addr(sV + st * kTileBytes), &tv, fb, 0, lc.h, lc.j * kKeys, lc.b);
+        mbar_expect_tx(smem_addr(&k_full[st]), kTileBytes);
+        tma_load_4d(smem_addr(sK + st * kTileBytes), &tk, smem_addr(&k_full[st]), 0, lc.h, lc.j * kKeys, lc.b);
+        if (lg >= kKvStages && !mbar_wait(smem_addr(&v_empty[st]), par)) {
+          ok = false;
+          break;
+        }
+        mbar_expect_tx(smem_addr(&v_full[st]), kTileBytes);
+        tma_load_4d(smem_addr(sV + st * kTileBytes), &tv, smem_addr(&v_full[st]), 0, lc.h, lc.j * kKeys, lc.b);
         lc.next(p);
         ++lg;
       }
@@ -242,7 +295,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           ++qs;
         }
         const int qslot = (qs - 1) & 1;
-        if (ok && !mbar_wait(smem_addr(&kv_full[st]), (uint32_t)((sg / kKvStages) & 1))) ok = false;
+        if (ok && !mbar_wait(smem_addr(&k_full[st]), (uint32_t)((sg / kKvStages) & 1))) ok = false;
         if (ok && sg > 0 && !mbar_wait(smem_addr(s_free), (uint32_t)((sg - 1) & 1))) ok = false;
         if (ok) {
           tc_fence_after();
@@ -253,6 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
             tc_mma(tm, qd + (uint64_t)(2 * k), kd + (uint64_t)(2 * k), idS, k > 0);
         }
         tc_commit(smem_addr(s_full));
+        tc_commit(smem_addr(&k_empty[st]));
         if (sc.last_in_tile()) tc_commit(smem_addr(&q_empty[qslot]));   // Q slot free once these MMAs retire
         sc.next(p);
         ++sg;
@@ -266,6 +320,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
           ++tiles_pv;
         }
         const int st = pg % kKvStages;
+        if (ok && !mbar_wait(smem_addr(&v_full[st]), (uint32_t)((pg / kKvStages) & 1))) ok = false;
         if (ok) {
           tc_fence_after();
           const uint64_t vd = desc_sw128(smem_addr(sV + st * kTileBytes));
@@ -275,7 +330,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                       (pc.j > 0 || kk > 0) ? 1u : 0u);
         }
         tc_commit(smem_addr(o_full));
-        tc_commit(smem_addr(&kv_empty[st]));
+        tc_commit(smem_addr(&v_empty[st]));
         pc.next(p);
         ++pg;
       }
@@ -295,18 +350,31 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       for (int j = 0; j < c.nblk; ++j, ++g) {
         if (!mbar_wait(smem_addr(s_full), (uint32_t)(g & 1))) ok = false;
         tc_fence_after();
+        // the whole S row in registers: one read of TMEM, after which the next S may overwrite it
+        uint32_t r[kKeys];
+#pragma unroll
+        for (int c2 = 0; c2 < kKeys; c2 += 32) tmem_ld32_nw(tS + (uint32_t)c2, r + c2);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(s_free));
         const int kbase = j * kKeys;
         // keys kbase .. kbase + nvalid - 1 are inside T and not after this row
         const int nvalid = min(p.T, j == c.nblk - 1 ? row + 1 : p.T) - kbase;
-        float mx = -INFINITY;
+        if (nvalid < kKeys) {
 #pragma unroll
-        for (int c2 = 0; c2 < kKeys; c2 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tS + (uint32_t)c2, r);
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (c2 + i < nvalid) mx = fmaxf(mx, __uint_as_float(r[i]));
+          for (int i = 0; i < kKeys; ++i)
+            if (i >= nvalid) r[i] = 0xff800000u;   // -inf: exponential 0
         }
+        // row max: 8 independent chains of 3-input maxima
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(__uint_as_float(r[i]), __uint_as_float(r[i + 8]));
+#pragma unroll
+        for (int i = 16; i < kKeys; i += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) m8[k] = fmax3(m8[k], __uint_as_float(r[i + k]), __uint_as_float(r[i + 8 + k]));
+        float mx = fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
         mx *= p.scale_log2;   // scale > 0 commutes with max
         bool rescale = false;
         float alpha = 1.f;
@@ -320,38 +388,38 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // P and O of the previous block are free once its PV has completed
         if (g > 0 && !mbar_wait(smem_addr(o_full), (uint32_t)((g - 1) & 1))) ok = false;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale)) {   // whole warp: tcgen05.ld / st are warp-wide
-          uint32_t r[32];
-#pragma unroll
-          for (int c2 = 0; c2 < kD; c2 += 32) {
-            tmem_ld32(tO + (uint32_t)c2, r);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st32(tO + (uint32_t)c2, r);
-          }
-          l *= alpha;
-        }
-        float rs = 0.f;
+        // P = 2^(S·scale - m): scale and offset as packed f32x2 FMAs, the row sum as packed adds
+        const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2), nm2 = pack_f2(-m_use, -m_use);
+        uint64_t acc2[2] = {0ull, 0ull};
 #pragma unroll
         for (int c2 = 0; c2 < kKeys; c2 += 32) {
-          uint32_t r[32];
-          tmem_ld32(tS + (uint32_t)c2, r);
-          if (c2 == kKeys - 32) {        // S fully read: the next S may overwrite it
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_addr(s_free));
-          }
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
-            const float p0 = c2 + 2 * i < nvalid ? ex2(fmaf(__uint_as_float(r[2 * i]), p.scale_log2, -m_use)) : 0.f;
-            const float p1 =
-                c2 + 2 * i + 1 < nvalid ? ex2(fmaf(__uint_as_float(r[2 * i + 1]), p.scale_log2, -m_use)) : 0.f;
-            rs += p0 + p1;
+            float x0, x1;
+            unpack_f2(ffma2(pack_u2(r[c2 + 2 * i], r[c2 + 2 * i + 1]), sc2, nm2), x0, x1);
+            const float p0 = ex2(x0), p1 = ex2(x1);
+            acc2[i & 1] = fadd2(acc2[i & 1], pack_f2(p0, p1));
             __nv_bfloat162 bp = __floats2bfloat162_rn(p0, p1);
             w[i] = *reinterpret_cast<uint32_t*>(&bp);
           }
           tmem_st16(tP + (uint32_t)(c2 / 2), w);
+        }
+        float s0, s1, s2, s3;
+        unpack_f2(acc2[0], s0, s1);
+        unpack_f2(acc2[1], s2, s3);
+        const float rs = (s0 + s1) + (s2 + s3);
+        // O rescale after P is written (S registers are dead by then)
+        if (__any_sync(0xffffffffu, rescale)) {   // whole warp: tcgen05.ld / st are warp-wide
+          uint32_t o[32];
+#pragma unroll
+          for (int c2 = 0; c2 < kD; c2 += 32) {
+            tmem_ld32(tO + (uint32_t)c2, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + (uint32_t)c2, o);
+          }
+          l *= alpha;
         }
         l += rs;
         tmem_wait_st();
