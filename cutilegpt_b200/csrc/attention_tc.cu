@@ -26,6 +26,12 @@
 // [B, H, T, D] layout are read in place; rows past T are zero-filled by TMA
 // and masked; the output tile leaves through a TMA store (rows past T
 // clipped). Every wait is bounded.
+#include <map>
+#include <memory>
+#include <queue>
+#include <tuple>
+#include <vector>
+
 #include "common.cuh"
 
 namespace gpt {
@@ -148,32 +154,81 @@ __device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t* r) {   //
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Bounded wait for the phase of the turn barrier, or until the other
+// pipeline has finished all its work (it then arrives no more).
+__device__ __noinline__ bool turn_wait(uint32_t bar, uint32_t parity, const volatile uint32_t* other_done) {
+  uint64_t t0 = 0;
+  for (int it = 0;; ++it) {
+    if (tc::mbar_try(bar, parity)) return true;
+    if (*other_done) return true;
+    if ((it & 31) == 31) {
+      const uint64_t t = global_timer_ns();
+      if (t0 == 0) {
+        t0 = t;
+      } else if (t - t0 > g_wait_limit_ns) {
+        record_device_error(GPT_DEVERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
 // Named barrier of one softmax warpgroup (ids 1, 2).
 __device__ __forceinline__ void wg_bar(int pipe) {
   asm volatile("bar.sync %0, 128;" ::"r"(1 + pipe) : "memory");
 }
 
-// Walks one pipeline's work: tiles t = first, first + stride, ... (tile t =
-// query block n_qblk-1 - t/(B*H) of head t%(B*H), heaviest first), and within
-// a tile the causal key blocks 0..qb.
+// Tile schedule: tile t is query block n_qblk-1 - t/(B*H) of head t%(B*H), so
+// tiles are numbered heaviest first (a tile costs its number of causal key
+// blocks). When the problem is small enough the host assigns the tiles to the
+// pipelines by longest-processing-time-first (each tile, heaviest first, to
+// the pipeline with the least work so far) and passes the lists here:
+// v[q] .. v[q+1]-1 index the tile ids of pipeline q in v[n_pipes + 1 + ...].
+// Otherwise (n == 0) pipeline q takes tiles q, q + n_pipes, q + 2 n_pipes, ...
+constexpr int kSchedMax = 4096;
+struct Sched {
+  int n;   // entries used in v (0: strided assignment)
+  uint16_t v[kSchedMax];
+};
+
+// Walks one pipeline's work, and within a tile the causal key blocks 0..qb.
 struct Cursor {
-  int tile, j, nblk, qb, b, h, stride;
+  int tile, j, nblk, qb, b, h;
+  int k, kend, q, n_pipes;
+  const uint16_t* list;
   bool valid;
-  __device__ void set(int t, const Params& p) {
-    tile = t;
+  __device__ void start(int pipe_id, int pipes, const Params& p, const Sched& s) {
+    q = pipe_id;
+    n_pipes = pipes;
+    if (s.n > 0) {
+      list = s.v + pipes + 1;
+      k = s.v[pipe_id];
+      kend = s.v[pipe_id + 1];
+    } else {
+      list = nullptr;
+      k = 0;
+      kend = 0x7fffffff;
+    }
+    load(p);
+  }
+  __device__ void load(const Params& p) {
     j = 0;
-    valid = t < p.n_tiles;
+    tile = list ? (k < kend ? (int)list[k] : p.n_tiles) : q + k * n_pipes;
+    valid = tile < p.n_tiles;
     if (valid) {
-      qb = p.n_qblk - 1 - t / p.BH;
-      const int bh = t % p.BH;
+      qb = p.n_qblk - 1 - tile / p.BH;
+      const int bh = tile % p.BH;
       b = bh / p.H;
       h = bh % p.H;
       nblk = qb + 1;
     }
   }
   __device__ bool last_in_tile() const { return j == nblk - 1; }
+  __device__ void next_tile(const Params& p) {
+    ++k;
+    load(p);
+  }
   __device__ void next(const Params& p) {
-    if (++j == nblk) set(tile + stride, p);
+    if (++j == nblk) next_tile(p);
   }
 };
 
@@ -181,7 +236,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
                                                               const __grid_constant__ CUtensorMap tk,
                                                               const __grid_constant__ CUtensorMap tv,
                                                               const __grid_constant__ CUtensorMap to,
-                                                              const Params p) {
+                                                              const Params p,
+                                                              const __grid_constant__ Sched sched) {
   extern __shared__ uint8_t smem_dyn[];
   uint8_t* base = (uint8_t*)(((uintptr_t)smem_dyn + 1023) & ~(uintptr_t)1023);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -204,7 +260,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   uint64_t* p_full = s_full + 2;                   // softmax warps: P written (and O rescaled)
   uint64_t* o_full = s_full + 3;                   // commit after PV
   uint64_t* o_free = s_full + 4;                   // softmax warps: final O read
+  uint64_t* turn_mine = s_full + 5;                // the other pipeline's exponentials are done
+  uint64_t* turn_other = (uint64_t*)(base + kPipes * kPipeBytes) + (1 - pipe) * 24 + 4 + 4 * kKvStages + 5;
   uint32_t* tmem_slot = (uint32_t*)((uint64_t*)(base + kPipes * kPipeBytes) + kPipes * 24);
+  volatile uint32_t* pipe_done = tmem_slot + 1;    // [kPipes]: a pipeline's softmax has finished
 
   if (tid == 0) {
     for (int q = 0; q < kPipes; ++q) {
@@ -216,7 +275,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       mbar_init(smem_addr(&sf[2]), 4);   // p_full
       mbar_init(smem_addr(&sf[3]), 1);   // o_full
       mbar_init(smem_addr(&sf[4]), 4);   // o_free
+      mbar_init(smem_addr(&sf[5]), 4);   // turn
     }
+    pipe_done[0] = 0;
+    pipe_done[1] = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
   }
@@ -233,15 +295,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
   pdl_wait();
   pdl_trigger();
   bool ok = true;
-  const int first = 2 * (int)blockIdx.x + pipe;
-  const int stride = 2 * (int)gridDim.x;
+  const int pipe_id = kPipes * (int)blockIdx.x + pipe, n_pipes = kPipes * (int)gridDim.x;
 
   if (warp >= 4 * kPipes + kPipes) {
     // ------------------------------------------------ TMA producer (one lane per pipeline)
     if (lane == 0) {
       Cursor lc;
-      lc.stride = stride;
-      lc.set(first, p);
+      lc.start(pipe_id, n_pipes, p, sched);
       int lg = 0, ql = 0;
       while (lc.valid && ok) {
         if (lc.j == 0) {
@@ -284,9 +344,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
       constexpr uint32_t idO = (1u << 4) | (1u << 7) | (1u << 10) | (1u << 16) | ((uint32_t)(kD >> 3) << 17) |
                                ((uint32_t)(kRows >> 4) << 24);
       Cursor sc, pc;                     // S-issue and PV-issue cursors
-      sc.stride = pc.stride = stride;
-      sc.set(first, p);
-      pc.set(first, p);
+      sc.start(pipe_id, n_pipes, p, sched);
+      pc.start(pipe_id, n_pipes, p, sched);
       int sg = 0, pg = 0, qs = 0, tiles_pv = 0;
       auto issue_s = [&]() {
         const int st = sg % kKvStages;
@@ -340,11 +399,10 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     const int rl = tid & (kRows - 1);
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t tS = tm + lane_off, tP = tm + 128 + lane_off, tO = tm + 192 + lane_off;
-    int g = 0;   // blocks of this pipeline so far
-    for (int t = first; t < p.n_tiles; t += stride) {
-      Cursor c;
-      c.stride = stride;
-      c.set(t, p);
+    int g = 0;       // blocks of this pipeline so far
+    int n_exp = 0;   // exponential phases of this pipeline so far
+    Cursor c;
+    for (c.start(pipe_id, n_pipes, p, sched); c.valid; c.next_tile(p)) {
       const int row = c.qb * kRows + rl;
       float m_use = -INFINITY, l = 0.f;
       for (int j = 0; j < c.nblk; ++j, ++g) {
@@ -388,6 +446,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // P and O of the previous block are free once its PV has completed
         if (g > 0 && !mbar_wait(smem_addr(o_full), (uint32_t)((g - 1) & 1))) ok = false;
         tc_fence_after();
+        // The two pipelines take turns at the exponentials (pipeline 0 first): while one computes
+        // its P, the other waits on its MMAs, so neither shares the issue slots and the
+        // special-function unit with the other's exponentials.
+        if (pipe == 1 || n_exp > 0) {
+          if (!turn_wait(smem_addr(turn_mine), (uint32_t)((pipe == 0 ? n_exp - 1 : n_exp) & 1),
+                         &pipe_done[1 - pipe]))
+            ok = false;
+        }
         // P = 2^(S·scale - m): scale and offset as packed f32x2 FMAs, the row sum as packed adds
         const uint64_t sc2 = pack_f2(p.scale_log2, p.scale_log2), nm2 = pack_f2(-m_use, -m_use);
         uint64_t acc2[2] = {0ull, 0ull};
@@ -409,6 +475,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         unpack_f2(acc2[0], s0, s1);
         unpack_f2(acc2[1], s2, s3);
         const float rs = (s0 + s1) + (s2 + s3);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(turn_other));
+        ++n_exp;
         // O rescale after P is written (S registers are dead by then)
         if (__any_sync(0xffffffffu, rescale)) {   // whole warp: tcgen05.ld / st are warp-wide
           uint32_t o[32];
@@ -459,6 +528,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         asm volatile("cp.async.bulk.commit_group;" ::: "memory");
       }
     }
+    if (lane == 0) pipe_done[pipe] = 1;   // the other pipeline no longer waits for its turn
     if (rl == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");  // output tiles written
   }
   tc_fence_before();
@@ -467,6 +537,45 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(*tmem_slot), "r"(512u));
   }
+}
+
+// Longest-processing-time-first assignment of the tiles to `pipes`
+// pipelines (cost of a tile: 2 per causal key block + 1 for its start and
+// output), cached per shape; n = 0 (strided assignment) when the lists do not
+// fit the kernel parameter.
+static const Sched& schedule(int BH, int n_qblk, int pipes) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, std::unique_ptr<Sched>> cache;
+  std::lock_guard<std::mutex> g(mu);
+  auto key = std::make_tuple(BH, n_qblk, pipes);
+  auto it = cache.find(key);
+  if (it != cache.end()) return *it->second;
+  auto sc = std::make_unique<Sched>();
+  sc->n = 0;
+  const int64_t n_tiles = (int64_t)BH * n_qblk;
+  if (n_tiles + pipes + 1 <= kSchedMax) {
+    using Load = std::pair<int64_t, int>;   // (work so far, pipeline), smallest first
+    std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+    for (int q = 0; q < pipes; ++q) heap.push({0, q});
+    std::vector<std::vector<int>> lists(pipes);
+    for (int64_t t = 0; t < n_tiles; ++t) {
+      Load l = heap.top();
+      heap.pop();
+      lists[l.second].push_back((int)t);
+      l.first += 2 * (n_qblk - t / BH) + 1;
+      heap.push(l);
+    }
+    int pos = 0;
+    for (int q = 0; q < pipes; ++q) {
+      sc->v[q] = (uint16_t)pos;
+      for (int t : lists[q]) sc->v[pipes + 1 + pos++] = (uint16_t)t;
+    }
+    sc->v[pipes] = (uint16_t)pos;
+    sc->n = pipes + 1 + pos;
+  }
+  const Sched& ref = *sc;
+  cache.emplace(key, std::move(sc));
+  return ref;
 }
 
 // 4-D map {D, H, T, B} over a bf16 tensor with element strides (sb, sh, st),
@@ -532,7 +641,8 @@ int launch(const void* q, const void* k, const void* v, void* out, int64_t B, in
   if (sms <= 0) sms = 148;
   const int64_t pairs = (tiles + kPipes - 1) / kPipes;
   const int grid = (int)(pairs < sms ? pairs : sms);   // persistent: one CTA per SM, two tiles in flight
-  launch_pdl(attn_tc_kernel, dim3((unsigned)grid), dim3(kThreads), kSmem, st, mq, mk, mv, mo, p);
+  const Sched& sc = schedule(p.BH, p.n_qblk, kPipes * grid);
+  launch_pdl(attn_tc_kernel, dim3((unsigned)grid), dim3(kThreads), kSmem, st, mq, mk, mv, mo, p, sc);
   return launch_status("attention_tc");
 }
 
