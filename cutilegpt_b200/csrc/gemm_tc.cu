@@ -611,7 +611,7 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
           uint16_t* C16 = reinterpret_cast<uint16_t*>(p.C);
           const int c_mis = (int)((reinterpret_cast<uintptr_t>(p.C) >> 1) & 7);
           if (colseg + kSeg <= p.N) {
-#pragma unroll 1
+#pragma unroll
             for (int rr0 = 0; rr0 < 32; rr0 += kRpi) {
               const int rr = rr0 + rsub;
               const int row = row0 + rr;
