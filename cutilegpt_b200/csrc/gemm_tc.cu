@@ -634,7 +634,9 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) w[i] = __funnelshift_r(t[i], t[i + 1], 16);
                   }
-                  *reinterpret_cast<uint4*>(C16 + g0 + e0) = make_uint4(w[0], w[1], w[2], w[3]);
+                  asm volatile("st.global.cs.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(C16 + g0 + e0), "r"(w[0]),
+                               "r"(w[1]), "r"(w[2]), "r"(w[3])
+                               : "memory");
                 }
                 // the (head + tail) = 8 edge elements when the segment is not aligned
                 if (head != 0) {
