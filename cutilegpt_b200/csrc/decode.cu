@@ -40,13 +40,14 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks) decode_kernel(const T
                                                              const T* __restrict__ vc, T* __restrict__ out,
                                                              int64_t ld_out, int H, int64_t Tmax, int L0,
                                                              const int64_t* __restrict__ len_dev,
-                                                             float scale_log2, float* __restrict__ ws) {
+                                                             float scale_log2, float* __restrict__ ws,
+                                                             int prefetch) {
   // Before the dependency wait: start pulling this CTA's cached K/V rows
   // into L2. Rows below the current position were written by earlier steps,
   // so the reads overlap the tail of the preceding kernel (the QKV GEMM that
   // appends row L-1). A prefetch is only a hint: the length read here may be
   // stale without affecting results, and is clamped to the cache.
-  {
+  if (prefetch) {
     int Lp = L0 + (len_dev ? (int)*reinterpret_cast<const volatile int64_t*>(len_dev) : 0);
     Lp = max(0, min(Lp, (int)Tmax));
     const int chunk = (Lp + gridDim.x - 1) / (int)gridDim.x;
@@ -238,8 +239,12 @@ static int launch(const void* q, int64_t ld_q, const void* kc, const void* vc, v
   if (sms <= 0) sms = 148;
   int ns = num_splits(B, H, len_dev ? Tmax : L, sms);
   dim3 grid((unsigned)ns, (unsigned)(B * H));
+  // The early L2 prefetch only pays while the launch's K/V fit comfortably in the 126 MB L2; a
+  // larger cache (long contexts, big batches) would be evicted before its main loads and read twice.
+  const int64_t kv_bytes = 2 * B * H * (len_dev ? Tmax : L) * (int64_t)D * (int64_t)sizeof(T);
+  const int prefetch = kv_bytes <= (int64_t(64) << 20) ? 1 : 0;
   launch_pdl(decode_kernel<T, D>, dim3(grid), dim3(kWarps * 32), 0, st, (const T*)q, ld_q, (const T*)kc, (const T*)vc, (T*)out,
-                                                    ld_out, (int)H, Tmax, (int)L, len_dev, sl2, (float*)ws);
+                                                    ld_out, (int)H, Tmax, (int)L, len_dev, sl2, (float*)ws, prefetch);
   int s = launch_status("attention_decode");
   if (s || ns == 1) return s;
   launch_pdl(combine_kernel<T, D>, dim3((unsigned)(B * H)), dim3(D), 0, st, (const float*)ws, ns, (T*)out, ld_out, (int)H);
