@@ -289,10 +289,11 @@ def test_argmax_edge_rows(dtype):
     x[3, V - 1] = 70.0                                             # last element
     x[4, :] = float("nan"); x[4, 12345] = -3.0                     # the only number wins
     x[6, 6282] = x[6, 6283] = x[6, 40000] = 80.0                    # tie across a wide-row chunk boundary
+    x[5, 2] = x[5, 10] = 90.0     # row 5 starts 5 elements into a 16-byte unit: tie between its head and a vector
     tok = torch.empty(7, dtype=torch.int64, device="cuda")
     ops.argmax(x.cuda(), tok)
     assert tok.cpu().tolist()[:5] == [5, 0, 777, V - 1, 12345]
-    assert tok[5].item() == x[5].float().argmax().item()
+    assert tok[5].item() == 2
     assert tok[6].item() == 6282
     small = randn(64, 3, seed=42).to(dtype)
     tok64 = torch.empty(64, dtype=torch.int64, device="cuda")
