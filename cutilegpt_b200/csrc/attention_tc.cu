@@ -41,6 +41,7 @@ using tc::desc_sw128;
 using tc::mbar_arrive;
 using tc::mbar_expect_tx;
 using tc::mbar_init;
+using tc::mbar_wait;
 using tc::smem_addr;
 using tc::tc_commit;
 using tc::tc_fence_after;
@@ -153,12 +154,6 @@ __device__ __forceinline__ void tmem_ld32_nw(uint32_t taddr, uint32_t* r) {   //
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
-// Bounded mbarrier wait with the first try inline (the common case: the
-// phase has completed already) and the bounded spin out of line.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  return tc::mbar_try(bar, parity) || tc::mbar_wait(bar, parity);
-}
-
 // Bounded wait for the phase of the turn barrier, or until the other
 // pipeline has finished all its work (it then arrives no more).
 __device__ __noinline__ bool turn_wait(uint32_t bar, uint32_t parity, const volatile uint32_t* other_done) {

@@ -95,7 +95,7 @@ __device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait for the phase with the given parity to complete.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+__device__ __noinline__ bool mbar_wait_spin(uint32_t bar, uint32_t parity) {
   if (mbar_try(bar, parity)) return true;
   uint64_t t0 = global_timer_ns();
   while (true) {
@@ -107,6 +107,10 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
       return false;
     }
   }
+}
+// First try inline (the phase has usually completed already), the bounded spin out of line.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  return mbar_try(bar, parity) || mbar_wait_spin(bar, parity);
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x,
                                             int y) {
