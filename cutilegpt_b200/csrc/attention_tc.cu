@@ -450,7 +450,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc_kernel(const __grid_const
         // its P, the other waits on its MMAs, so neither shares the issue slots and the
         // special-function unit with the other's exponentials.
         if (pipe == 1 || n_exp > 0) {
-          if (!turn_wait(smem_addr(turn_mine), (uint32_t)((pipe == 0 ? n_exp - 1 : n_exp) & 1),
+          if (!tc::mbar_try(smem_addr(turn_mine), (uint32_t)((pipe == 0 ? n_exp - 1 : n_exp) & 1)) &&
+              !turn_wait(smem_addr(turn_mine), (uint32_t)((pipe == 0 ? n_exp - 1 : n_exp) & 1),
                          &pipe_done[1 - pipe]))
             ok = false;
         }
