@@ -376,6 +376,7 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      const uint64_t ad0 = desc_sw128(smem_addr(ringA)), bd0 = desc_sw128(smem_addr(ringB));
       for (int tile = first_tile; tile < p.num_tiles && ok; tile += tile_step) {
         if (!mbar_wait(smem_addr(&tempty[acc]), acc_phase ^ 1)) break;
         tc_fence_after();
@@ -383,8 +384,9 @@ __global__ void __launch_bounds__((2 + epi_warps(kTmaStore)) * 32, 1)
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(smem_addr(&full[stage]), phase)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t ad = desc_sw128(smem_addr(ringA + stage * S::kABytes));
-          const uint64_t bd = desc_sw128(smem_addr(ringB + stage * S::kBBytes));
+          // descriptors of this stage: the address field (bytes >> 4) offset from stage 0
+          const uint64_t ad = ad0 + (uint64_t)(stage * (S::kABytes >> 4));
+          const uint64_t bd = bd0 + (uint64_t)(stage * (S::kBBytes >> 4));
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             // +32 bytes per K=16 step inside the swizzle atom (encoded >>4).
